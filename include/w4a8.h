@@ -1,0 +1,175 @@
+/*
+ * webyIQ W4A8 quantized-matmul hot path for NVIDIA B200 (sm_100a): the C ABI.
+ *
+ * This is the drop-in boundary for the operator surface of the webyIQ engine
+ * (crates/engine/src/graph.rs:190-222, 476-486): the int4-weight x int8-activation
+ * GEMV (decode and MTP verify), the prefill GEMM, the activation quantizer
+ * (optionally fused with RMSNorm) and the greedy argmax over lm_head logits.
+ *
+ * Conventions
+ *  - Every pointer argument except `w4a8_weight_view`'s output struct and the
+ *    workspace-size queries is a DEVICE pointer owned by the caller.  Nothing is
+ *    allocated, freed or copied between host and device inside these calls, and
+ *    no call synchronizes the host: every launch is ordered on `stream`
+ *    (a cudaStream_t passed as void*; NULL = the legacy default stream).
+ *  - Errors are returned as a w4a8_status; w4a8_last_error() gives a message for
+ *    the calling thread.  Shapes, modes and pointer alignment are validated on the
+ *    host before any launch, so an EINVAL call launches nothing.
+ *  - Calls on distinct streams are thread-safe.
+ *
+ * Weight layout (tools/convert.py:7-12, 68-75 of the reference): a quantized linear
+ * weight with n output rows and k inputs is
+ *   q : u32[n, k/8]   word i of a row holds weights 8i..8i+7 with
+ *                      byte b = w[8i+b] | w[8i+4+b] << 4   (nibbles are unsigned 0..15)
+ *   s : has_min = 1 -> u32[n, k/group]  = f16 scale | f16 min << 16,  w = q*scale + min
+ *       has_min = 0 -> f16[n, k/group]  = scale,                       w = (q-8)*scale
+ * has_min = 1 with group 32 is exactly what convert.py / gptq.py write.  has_min = 0
+ * is the symmetric signed-int4 format (values -8..7 stored as q-8 nibbles).
+ *
+ * Activation layout (crates/engine/src/shaders/quant.wgsl:1-4, 41-61): xq is int8[m, k]
+ * (row = token).  Its scales `xs` come in two layouts:
+ *   W4A8_ACT_GROUP32 : f32[m, k/32, 2] = (dx, dx * sum(xq)) per 32 inputs (the engine's)
+ *   W4A8_ACT_TOKEN   : f32[m]          = dx per token (per-row absmax)
+ *
+ * Numerics.  The int32 dot product of every (token, row, group) is exact.  With
+ * W4A8_ACT_TOKEN the whole row sum is exact as well: every group term
+ * scale*I + min*sum(xq) is an integer multiple of 2^-24 (f16 scales are), it is
+ * accumulated in int64, and the output is ((float)acc * 2^-24) * dx, rounded twice
+ * and independent of how the work was split.  So results are bit-identical across
+ * the GEMV, the GEMM, any grid size and any number of GPUs, and the argmax ids are
+ * exact.  The accumulator cannot overflow while k * 1905 * (|scale| + |min|) < 2^39
+ * for every group (for k = 8192: |scale| + |min| < 35000).  With W4A8_ACT_GROUP32 the
+ * group terms s*dx*I + m*dxsum are accumulated in f32 (as gemv_q4q8.wgsl:68 does),
+ * so results agree with any other order to f32 rounding.
+ */
+#ifndef WEBYIQ_W4A8_H
+#define WEBYIQ_W4A8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define W4A8_API __attribute__((visibility("default")))
+#else
+#define W4A8_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum w4a8_status {
+    W4A8_OK = 0,
+    W4A8_EINVAL = 1,   /* shape, mode, alignment or pointer rejected; nothing launched */
+    W4A8_ECUDA = 2,    /* a CUDA runtime call or launch failed */
+    W4A8_ENCCL = 3,    /* an NCCL call failed */
+    W4A8_ETIMEOUT = 4, /* a bounded device-side wait gave up */
+    W4A8_ENOTSUP = 5   /* a valid request this build does not implement */
+} w4a8_status;
+
+/* activation scale layouts */
+enum { W4A8_ACT_GROUP32 = 0, W4A8_ACT_TOKEN = 1 };
+
+/* output modes: MODE of gemv_q4q8.wgsl:4 / gemm_q4q8.wgsl:3 */
+enum {
+    W4A8_STORE = 0,  /* y = W x */
+    W4A8_ADD = 1,    /* y += W x (residual) */
+    W4A8_SWIGLU = 2  /* y[j] = silu(W[j] x) * W[j + n/2] x, output width n/2 */
+};
+
+/* largest token count the GEMV takes; larger batches go to the GEMM */
+#define W4A8_GEMV_MAX_M 16
+
+typedef struct w4a8_weight {
+    const void* q;   /* device u32[n, k/8] */
+    const void* s;   /* device, see the header comment */
+    int32_t n;       /* rows (output channels) of the stored tensor */
+    int32_t k;       /* inputs */
+    int32_t group;   /* 32 or 128 */
+    int32_t has_min; /* 1: (scale, min) pairs; 0: symmetric, scale only */
+} w4a8_weight;
+
+/* Describe a quantized weight already in device memory (no copy, no allocation).
+ * Replaces the binding of `{w}.q` / `{w}.s` in Builder::gemv / Builder::gemm
+ * (graph.rs:192-204) and the q4 checks of Manifest::parse (manifest.rs:82).
+ * Checks: group in {32, 128}; k % group == 0; n >= 1; q 16-byte aligned; s 4-byte
+ * aligned (has_min) or 2-byte aligned. */
+W4A8_API w4a8_status w4a8_weight_view(const void* q, const void* s, int32_t n, int32_t k, int32_t group,
+                             int32_t has_min, w4a8_weight* out);
+
+/* Activation quantization, optionally fused with RMSNorm (quant.wgsl:19-62,
+ * Builder::quant graph.rs:216-222):
+ *   v = norm_w ? x * (1/sqrt(mean(x^2) + eps)) * norm_w : x
+ *   GROUP32: per 32 inputs  dx = amax/127, xq = rint(v * (1/dx)), xs = (dx, dx*sum xq)
+ *   TOKEN  : per row        dx = amax/127, xq = rint(v * (1/dx)), xs = dx
+ * (amax == 0 gives dx = 0 and xq = 0.)  x f32[m, k], norm_w f32[k] or NULL.
+ * Needs k % 32 == 0, x and norm_w 16-byte aligned, xq 16-byte aligned. */
+W4A8_API w4a8_status w4a8_quant(const float* x, const float* norm_w, float eps, int32_t m, int32_t k,
+                       int32_t act, int8_t* xq, float* xs, void* stream);
+
+/* Decode / verify GEMV, m in [1, W4A8_GEMV_MAX_M] tokens (gemv_q4q8.wgsl:36-131,
+ * Builder::gemv graph.rs:190-198).  y f32[m, n] (n/2 for SWIGLU), token stride n
+ * (n/2).  xq 16-byte aligned. */
+W4A8_API w4a8_status w4a8_gemv(const w4a8_weight* w, const int8_t* xq, const float* xs, int32_t act,
+                      int32_t m, int32_t mode, float* y, void* stream);
+
+/* Prefill GEMM Y[m, n] = X W^T for any m >= 1 (gemm_q4q8.wgsl:46-121,
+ * Builder::gemm graph.rs:200-205). */
+W4A8_API w4a8_status w4a8_gemm(const w4a8_weight* w, const int8_t* xq, const float* xs, int32_t act,
+                      int32_t m, int32_t mode, float* y, void* stream);
+
+/* Builder::matmul (graph.rs:207-214): the GEMV for m <= W4A8_GEMV_MAX_M, the GEMM
+ * above that. */
+W4A8_API w4a8_status w4a8_matmul(const w4a8_weight* w, const int8_t* xq, const float* xs, int32_t act,
+                        int32_t m, int32_t mode, float* y, void* stream);
+
+/* Greedy sampling over f32 logits[m, v] (argmax.wgsl:14-43): tok_out[r] is the lowest
+ * index among the maxima of row r, over values > -3e38 (NaN never wins; a row with
+ * no such value gives 0).  ids (u32[v]) or NULL: with ids, tok_out[r] = ids[index]. */
+W4A8_API w4a8_status w4a8_argmax(const float* logits, int32_t m, int32_t v, const uint32_t* ids,
+                        uint32_t* tok_out, void* stream);
+
+/* lm_head GEMV with fused argmax (head_ops, graph.rs:476-486, fused): for each token
+ * r, best_key[r] = the packed key of the argmax over this weight's rows, with global
+ * row ids row_offset + j (row_offset = this shard's first vocabulary row when the
+ * vocabulary is split across GPUs).  Keys compare as unsigned integers, so the max
+ * of the shard keys is the key of the global argmax: see w4a8_key_index.
+ * logits (f32[m, n]) may be NULL to skip writing them; tok_out (u32[m]) may be NULL;
+ * ids as in w4a8_argmax (indexed by the global row id).  mode is always STORE.
+ * workspace: w4a8_lmhead_workspace_bytes(n, m) bytes of device memory, zero-filled
+ * before its first use; every call leaves it zero-filled again.  Calls that share a
+ * workspace must not overlap on the GPU. */
+W4A8_API w4a8_status w4a8_lmhead_argmax(const w4a8_weight* w, int32_t row_offset, const int8_t* xq,
+                               const float* xs, int32_t act, int32_t m, float* logits,
+                               uint64_t* best_key, uint32_t* tok_out, const uint32_t* ids,
+                               void* workspace, size_t workspace_bytes, void* stream);
+W4A8_API size_t w4a8_lmhead_workspace_bytes(int32_t n, int32_t m);
+
+/* Index carried by a packed argmax key (0 for the "no value > -3e38" key 0). */
+static inline uint32_t w4a8_key_index(uint64_t key) {
+    return key ? ~(uint32_t)(key & 0xffffffffu) : 0u;
+}
+
+/* Test hook: the exact int32 dot product of every (token, row, group),
+ * dots[t, j, g] = sum over the group of q'[j, i] * xq[t, i], with q' = q (has_min)
+ * or q - 8 (symmetric), computed by the GEMV's own load / unpack / dp4a path.
+ * dots int32[m, n, k/group], m in [1, W4A8_GEMV_MAX_M]. */
+W4A8_API w4a8_status w4a8_group_dots(const w4a8_weight* w, const int8_t* xq, int32_t m, int32_t* dots,
+                            void* stream);
+
+/* Tuning: enable (default) or disable programmatic dependent launch, which lets a
+ * kernel's CTAs start (and prefetch weights) while the previous kernel in the
+ * stream drains.  Process-wide. */
+W4A8_API void w4a8_set_pdl(int enable);
+
+/* Message for the last failed call on this thread ("" if none). */
+W4A8_API const char* w4a8_last_error(void);
+
+/* Build identification string. */
+W4A8_API const char* w4a8_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WEBYIQ_W4A8_H */

@@ -1,0 +1,105 @@
+"""CPU: the C-ABI library loads, exports every symbol include/w4a8.h declares, and
+rejects bad arguments on the host before any launch (no GPU needed)."""
+
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+from webyiq_b200 import _lib, fmt
+
+
+def test_library_exports_header_symbols():
+    L = _lib.load()
+    syms = _lib.header_symbols()
+    assert len(syms) >= 12
+    for name in syms:
+        assert hasattr(L, name), name
+    assert b"sm_100a" in L.w4a8_version()
+
+
+def test_sigs_cover_header():
+    assert sorted(_lib._SIGS) == _lib.header_symbols()
+
+
+def _view(q=16, s=16, n=8, k=256, group=32, has_min=1):
+    w = _lib.Weight()
+    st = _lib.load().w4a8_weight_view(ctypes.c_void_p(q), ctypes.c_void_p(s), n, k, group, has_min, ctypes.byref(w))
+    return st, w
+
+
+def test_weight_view_validation():
+    st, w = _view()
+    assert st == _lib.OK and w.n == 8 and w.k == 256 and w.group == 32 and w.has_min == 1
+    for kw in (dict(group=64), dict(k=100), dict(k=96, group=128), dict(n=0), dict(q=8), dict(s=2),
+               dict(q=0)):
+        st, _ = _view(**kw)
+        assert st == _lib.EINVAL, kw
+        assert _lib.load().w4a8_last_error()
+    st, _ = _view(s=2, has_min=0)  # f16 scales need only 2-byte alignment
+    assert st == _lib.OK
+
+
+def test_calls_reject_bad_arguments_before_launch():
+    L = _lib.load()
+    _, w = _view()
+    P = ctypes.c_void_p
+    # m out of range, bad mode, misaligned xq, NULL y: all EINVAL, nothing launched
+    assert L.w4a8_gemv(ctypes.byref(w), P(16), P(16), 0, 0, 0, P(16), None) == _lib.EINVAL
+    assert L.w4a8_gemv(ctypes.byref(w), P(16), P(16), 0, 17, 0, P(16), None) == _lib.EINVAL
+    assert L.w4a8_gemv(ctypes.byref(w), P(16), P(16), 0, 1, 3, P(16), None) == _lib.EINVAL
+    assert L.w4a8_gemv(ctypes.byref(w), P(17), P(16), 0, 1, 0, P(16), None) == _lib.EINVAL
+    assert L.w4a8_gemv(ctypes.byref(w), P(16), P(16), 0, 1, 0, None, None) == _lib.EINVAL
+    assert L.w4a8_gemv(ctypes.byref(w), P(16), P(16), 2, 1, 0, P(16), None) == _lib.EINVAL
+    assert L.w4a8_quant(P(16), None, 1e-6, 1, 100, 0, P(16), P(16), None) == _lib.EINVAL
+    assert L.w4a8_quant(P(16), P(4), 1e-6, 1, 128, 0, P(16), P(16), None) == _lib.EINVAL
+    assert L.w4a8_argmax(P(16), 0, 10, None, P(16), None) == _lib.EINVAL
+    ws = L.w4a8_lmhead_workspace_bytes(8, 1)
+    assert ws >= 136
+    assert L.w4a8_lmhead_argmax(ctypes.byref(w), 0, P(16), P(16), 1, 1, None, P(16), None, None, P(16), 8,
+                                None) == _lib.EINVAL
+    assert L.w4a8_lmhead_argmax(ctypes.byref(w), -1, P(16), P(16), 1, 1, None, P(16), None, None, P(16), ws,
+                                None) == _lib.EINVAL
+    assert b"row_offset" in L.w4a8_last_error()
+
+
+def test_manifest_roundtrip_and_faults(tmp_path):
+    codes = np.random.default_rng(0).integers(0, 16, (16, 64), dtype=np.uint32)
+    q = fmt.pack_nibbles(codes)
+    s = fmt.scale_words(np.full((16, 2), 0.01, np.float16), np.full((16, 2), -0.08, np.float16))
+    path = fmt.write_model(str(tmp_path / "m"), {"lin.q": (q, "q4", (16, 64)), "lin.s": (s, "q4s", (16, 2)),
+                                                 "norm": (np.ones(64, np.float32), "f32", (64,))})
+    m = fmt.Manifest(path)
+    q2, s2, n, k, g = m.q4("lin")
+    np.testing.assert_array_equal(q2, q)
+    np.testing.assert_array_equal(s2, s)
+    assert (n, k, g) == (16, 64, 32)
+    assert all(t["offset"] % 256 == 0 for t in m.tensors.values())
+    # corrupt manifests are rejected like Manifest::parse (manifest.rs:77-86)
+    import json
+
+    raw = json.load(open(path))
+    for bad in ({"format": "webyiq-v1"}, {"arch": "gpt2"}, {"quant": {"bits": 4, "group": 64, "scheme": "x"}}):
+        d = dict(raw, **bad)
+        p = tmp_path / "bad.json"
+        p.write_text(json.dumps(d))
+        with pytest.raises(ValueError):
+            fmt.Manifest(str(p))
+    # a truncated shard is detected on read
+    shard = tmp_path / "m" / "shard-000.bin"
+    data = shard.read_bytes()
+    shard.write_bytes(data[: len(data) // 2])
+    with pytest.raises(ValueError):
+        fmt.Manifest(path).q4("lin")
+
+
+def test_product_has_no_oracle_dependency():
+    """The shipped package never imports the test oracle."""
+    pkg = os.path.join(os.path.dirname(os.path.dirname(__file__)), "webyiq_b200")
+    for root, _, files in os.walk(pkg):
+        for f in files:
+            if f.endswith((".py", ".cu", ".cuh", ".cpp", ".h")):
+                text = open(os.path.join(root, f)).read()
+                for needle in ("import oracle", "from oracle", "liboracle", "orc_"):
+                    assert needle not in text, (f, needle)

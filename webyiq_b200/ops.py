@@ -1,0 +1,154 @@
+"""The engine's operator surface on torch CUDA tensors, over the C ABI.
+
+Mirrors crates/engine/src/graph.rs: Builder::gemv (:190-198), Builder::gemm
+(:200-205), Builder::matmul (:207-214), Builder::quant (:216-222) and the argmax op
+of head_ops (:478-486), plus the fused lm_head argmax.  Every call launches on
+torch's current CUDA stream and returns without synchronizing; arguments are
+checked by the library (W4A8Error with status EINVAL before any launch).
+"""
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import ACT_GROUP32, ACT_TOKEN, ADD, GEMV_MAX_M, STORE, SWIGLU  # noqa: F401
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and (not t.is_cuda or not t.is_contiguous()):
+            raise ValueError("webyiq_b200 ops take contiguous CUDA tensors")
+
+
+class QWeight:
+    """A quantized linear weight in device memory, in the reference's layout.
+
+    q: int32/uint32 tensor [n, k/8] (the u32 words of `{w}.q`);
+    s: has_min -> int32/uint32 [n, k/group] (`{w}.s`: f16 scale | f16 min << 16),
+       else float16/int16 [n, k/group] (scale only, w = (q-8)*scale).
+    """
+
+    def __init__(self, q, s, n, k, group, has_min):
+        _need_cuda(q, s)
+        self.q, self.s = q, s
+        self.n, self.k, self.group, self.has_min = int(n), int(k), int(group), int(bool(has_min))
+        self.c = _lib.Weight()
+        _lib.check(_lib.load().w4a8_weight_view(_ptr(q), _ptr(s), self.n, self.k, self.group, self.has_min,
+                                                ctypes.byref(self.c)))
+
+    def __repr__(self):
+        return f"QWeight(n={self.n}, k={self.k}, group={self.group}, has_min={self.has_min})"
+
+
+def xs_shape(m, k, act):
+    return (m,) if act == ACT_TOKEN else (m, k // 32, 2)
+
+
+def quant(x, norm_w=None, eps=1e-6, act=ACT_GROUP32, xq=None, xs=None):
+    """int8 activation quantization of the rows of x f32 [m, k], optionally
+    RMSNorm'ed with norm_w (quant.wgsl).  Returns (xq int8 [m, k], xs f32)."""
+    _need_cuda(x, norm_w)
+    m, k = x.shape
+    if xq is None:
+        xq = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    if xs is None:
+        xs = torch.empty(xs_shape(m, k, act), dtype=torch.float32, device=x.device)
+    _lib.check(_lib.load().w4a8_quant(_ptr(x), _ptr(norm_w), float(eps), m, k, act, _ptr(xq), _ptr(xs), _stream()))
+    return xq, xs
+
+
+def _out(w, m, mode, y, device):
+    n_out = w.n // 2 if mode == SWIGLU else w.n
+    if y is None:
+        if mode == ADD:
+            raise ValueError("mode ADD needs y")
+        y = torch.empty((m, n_out), dtype=torch.float32, device=device)
+    return y
+
+
+def gemv(w, xq, xs, act=ACT_GROUP32, mode=STORE, y=None):
+    """y (+)= W x for m <= 16 tokens (gemv_q4q8.wgsl)."""
+    _need_cuda(xq, xs, y)
+    m = xq.shape[0]
+    y = _out(w, m, mode, y, xq.device)
+    _lib.check(_lib.load().w4a8_gemv(ctypes.byref(w.c), _ptr(xq), _ptr(xs), act, m, mode, _ptr(y), _stream()))
+    return y
+
+
+def gemm(w, xq, xs, act=ACT_GROUP32, mode=STORE, y=None):
+    """Y (+)= X W^T for any m (gemm_q4q8.wgsl)."""
+    _need_cuda(xq, xs, y)
+    m = xq.shape[0]
+    y = _out(w, m, mode, y, xq.device)
+    _lib.check(_lib.load().w4a8_gemm(ctypes.byref(w.c), _ptr(xq), _ptr(xs), act, m, mode, _ptr(y), _stream()))
+    return y
+
+
+def matmul(w, xq, xs, act=ACT_GROUP32, mode=STORE, y=None):
+    """GEMV for m <= 16 tokens, GEMM above (Builder::matmul)."""
+    _need_cuda(xq, xs, y)
+    m = xq.shape[0]
+    y = _out(w, m, mode, y, xq.device)
+    _lib.check(_lib.load().w4a8_matmul(ctypes.byref(w.c), _ptr(xq), _ptr(xs), act, m, mode, _ptr(y), _stream()))
+    return y
+
+
+def argmax(logits, ids=None, out=None):
+    """Greedy token of every row of logits f32 [m, v] (argmax.wgsl)."""
+    _need_cuda(logits, ids, out)
+    m, v = logits.shape
+    if out is None:
+        out = torch.empty(m, dtype=torch.int32, device=logits.device)
+    _lib.check(_lib.load().w4a8_argmax(_ptr(logits), m, v, _ptr(ids), _ptr(out), _stream()))
+    return out
+
+
+def group_dots(w, xq):
+    """Exact int32 dot of every (token, row, group): int32 [m, n, k/group]."""
+    _need_cuda(xq)
+    m = xq.shape[0]
+    dots = torch.empty((m, w.n, w.k // w.group), dtype=torch.int32, device=xq.device)
+    _lib.check(_lib.load().w4a8_group_dots(ctypes.byref(w.c), _ptr(xq), m, _ptr(dots), _stream()))
+    return dots
+
+
+def lmhead_workspace(w, m, device):
+    nbytes = _lib.load().w4a8_lmhead_workspace_bytes(w.n, m)
+    return torch.zeros(nbytes, dtype=torch.uint8, device=device)
+
+
+def lmhead_argmax(w, xq, xs, act=ACT_TOKEN, row_offset=0, logits=None, ids=None, workspace=None,
+                  best_key=None, tok=None):
+    """lm_head GEMV with fused argmax.  Returns (best_key int64 [m] (u64 bits), tok int32 [m])."""
+    _need_cuda(xq, xs, logits, ids, workspace)
+    m = xq.shape[0]
+    dev = xq.device
+    if workspace is None:
+        workspace = lmhead_workspace(w, m, dev)
+    if best_key is None:
+        best_key = torch.empty(m, dtype=torch.int64, device=dev)
+    if tok is None:
+        tok = torch.empty(m, dtype=torch.int32, device=dev)
+    _lib.check(_lib.load().w4a8_lmhead_argmax(ctypes.byref(w.c), int(row_offset), _ptr(xq), _ptr(xs), act, m,
+                                              _ptr(logits), _ptr(best_key), _ptr(tok), _ptr(ids), _ptr(workspace),
+                                              workspace.numel(), _stream()))
+    return best_key, tok
+
+
+def key_index(key):
+    """Index carried by a packed argmax key (python int, u64 bits)."""
+    key &= (1 << 64) - 1
+    return (~key) & 0xFFFFFFFF if key else 0
+
+
+def set_pdl(enable):
+    _lib.load().w4a8_set_pdl(1 if enable else 0)
