@@ -93,7 +93,7 @@ typedef struct w4a8_weight {
  * Replaces the binding of `{w}.q` / `{w}.s` in Builder::gemv / Builder::gemm
  * (graph.rs:192-204) and the q4 checks of Manifest::parse (manifest.rs:82).
  * Checks: group in {32, 128}; k % group == 0; n >= 1; q 16-byte aligned; s 4-byte
- * aligned (has_min) or 2-byte aligned. */
+ * aligned (every tensor of a converted model is 256-byte aligned, convert.py:24). */
 W4A8_API w4a8_status w4a8_weight_view(const void* q, const void* s, int32_t n, int32_t k, int32_t group,
                              int32_t has_min, w4a8_weight* out);
 
@@ -161,6 +161,18 @@ W4A8_API w4a8_status w4a8_group_dots(const w4a8_weight* w, const int8_t* xq, int
  * kernel's CTAs start (and prefetch weights) while the previous kernel in the
  * stream drains.  Process-wide. */
 W4A8_API void w4a8_set_pdl(int enable);
+
+/* Tuning / testing: route group-128 per-token GEMVs to the tensor-core kernel
+ * (1, default) or to the dp4a kernel (0).  Both give bit-identical results.
+ * Process-wide. */
+W4A8_API void w4a8_set_gemv_kernel(int tensor_core);
+
+/* Device-side error word: every wait inside a kernel (for a TMA copy to land) is
+ * bounded; a wait that gives up records a code here and the kernel returns
+ * without touching its outputs.  This call synchronizes `stream`, returns
+ * W4A8_ETIMEOUT and the code if any was recorded (and clears it), else W4A8_OK.
+ * code may be NULL. */
+W4A8_API w4a8_status w4a8_device_error(uint32_t* code, void* stream);
 
 /* Message for the last failed call on this thread ("" if none). */
 W4A8_API const char* w4a8_last_error(void);

@@ -37,7 +37,7 @@ def test_weight_view_validation():
         st, _ = _view(**kw)
         assert st == _lib.EINVAL, kw
         assert _lib.load().w4a8_last_error()
-    st, _ = _view(s=2, has_min=0)  # f16 scales need only 2-byte alignment
+    st, _ = _view(s=4, has_min=0)
     assert st == _lib.OK
 
 

@@ -267,3 +267,25 @@ def test_device_pointer_errors(cuda):
     xs = torch.ones(1, dtype=torch.float32, device=cuda)
     with pytest.raises(W4A8Error, match="aligned"):
         ops.gemv(w, xq[1:].view(1, 256), xs, act=1)
+
+
+@pytest.mark.parametrize("has_min", [False, True])
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 13, 16])
+@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("nk", [(200, 2048), (64, 6144), (48, 1024), (24, 256)])
+def test_tensor_core_and_dp4a_kernels_agree(cuda, has_min, m, mode, nk):
+    """Group-128 per-token GEMVs run on the tensor-core kernel by default; the dp4a
+    kernel computes the same exact sums, so both must agree bit for bit."""
+    n, k = nk
+    q, s, _ = make_weight(n, k, 128, has_min, seed=n + m + mode)
+    xq, xs = orc.quant(make_x(m, k, seed=m), act=1)
+    w = dev_weight(q, s, n, k, 128, has_min, cuda)
+    base = make_x(m, n // 2 if mode == 2 else n, seed=7)
+    outs = []
+    for tc in (True, False):
+        ops.set_gemv_kernel(tc)
+        y = to_dev(base, cuda) if mode == 1 else None
+        outs.append(ops.gemv(w, to_dev(xq, cuda), to_dev(xs, cuda), act=1, mode=mode, y=y).cpu().numpy())
+    ops.set_gemv_kernel(True)
+    np.testing.assert_array_equal(bits(outs[0]), bits(outs[1]))
+    assert ops.device_error() == 0

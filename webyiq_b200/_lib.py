@@ -43,6 +43,8 @@ _SIGS = {
     "w4a8_lmhead_workspace_bytes": (ctypes.c_size_t, [_I, _I]),
     "w4a8_group_dots": (ctypes.c_int, [ctypes.POINTER(Weight), _P, _I, _P, _P]),
     "w4a8_set_pdl": (None, [ctypes.c_int]),
+    "w4a8_set_gemv_kernel": (None, [ctypes.c_int]),
+    "w4a8_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), _P]),
     "w4a8_last_error": (ctypes.c_char_p, []),
     "w4a8_version": (ctypes.c_char_p, []),
 }
@@ -61,7 +63,7 @@ def load(path=None):
     global _lib
     if _lib is not None:
         return _lib
-    path = path or LIB_PATH
+    path = path or os.environ.get("WEBYIQ_W4A8_LIB") or LIB_PATH
     if not os.path.exists(path):
         raise RuntimeError(f"webyiq_b200 CUDA library not built ({path}); run `python -m webyiq_b200.build`")
     L = ctypes.CDLL(path)

@@ -16,13 +16,14 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
-BUILD = os.path.join(HERE, "_build")
+BUILD = os.environ.get("W4A8_BUILD_DIR", os.path.join(HERE, "_build"))
 LIBDIR = os.path.join(HERE, "lib")
-LIB = os.path.join(LIBDIR, "libwebyiq_w4a8.so")
+LIB = os.environ.get("W4A8_LIB_OUT", os.path.join(LIBDIR, "libwebyiq_w4a8.so"))
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", f"-I{os.path.join(ROOT, 'include')}"]
+FLAGS += os.environ.get("W4A8_NVCC_FLAGS", "").split()
 
 
 def _headers_digest():
@@ -56,11 +57,16 @@ def _compile(src, digest, verbose):
 def build(verbose=False, jobs=None):
     """Compile csrc/*.cu for sm_100a and link the shared library; returns its path."""
     os.makedirs(BUILD, exist_ok=True)
-    os.makedirs(LIBDIR, exist_ok=True)
+    os.makedirs(os.path.dirname(LIB), exist_ok=True)
     digest = _headers_digest()
     srcs = sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
     with cf.ThreadPoolExecutor(max_workers=jobs or os.cpu_count()) as ex:
         objs = list(ex.map(lambda s: _compile(s, digest, verbose), srcs))
+    keep = set(objs)
+    for fn in os.listdir(BUILD):  # drop objects of earlier sources
+        path = os.path.join(BUILD, fn)
+        if path not in keep and fn.endswith(".o"):
+            os.remove(path)
     link_key = hashlib.sha256("".join(objs).encode()).hexdigest()[:16]
     stamp = LIB + ".stamp"
     if os.path.exists(LIB) and os.path.exists(stamp) and open(stamp).read() == link_key:

@@ -12,9 +12,11 @@
 namespace w4a8 {
 
 int g_use_pdl = 1;
+int g_use_mma = 1;
 
 namespace {
 thread_local char t_err[512] = "";
+}  // namespace
 
 int sm_count() {
     static int counts[64] = {0};
@@ -28,6 +30,7 @@ int sm_count() {
     return counts[dev];
 }
 
+namespace {
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 }  // namespace
 
@@ -45,19 +48,23 @@ w4a8_status check_launch(const char* what) {
     return W4A8_OK;
 }
 
-w4a8_status launch_gemv_g32_m0(const GemvParams&, int, int, int, int, int, cudaStream_t);
-w4a8_status launch_gemv_g32_m1(const GemvParams&, int, int, int, int, int, cudaStream_t);
-w4a8_status launch_gemv_g128_m0(const GemvParams&, int, int, int, int, int, cudaStream_t);
-w4a8_status launch_gemv_g128_m1(const GemvParams&, int, int, int, int, int, cudaStream_t);
+w4a8_status launch_gemv_g32_m0(const GemvParams&, int, int, int, cudaStream_t);
+w4a8_status launch_gemv_g32_m1(const GemvParams&, int, int, int, cudaStream_t);
+w4a8_status launch_gemv_g128_m0(const GemvParams&, int, int, int, cudaStream_t);
+w4a8_status launch_gemv_g128_m1(const GemvParams&, int, int, int, cudaStream_t);
 w4a8_status launch_quant(const float*, const float*, float, int, int, int, int8_t*, float*, cudaStream_t);
 w4a8_status launch_argmax(const float*, int, int, const uint32_t*, uint32_t*, cudaStream_t);
 
-w4a8_status launch_gemv(const GemvParams& p, int group, bool has_min, int act, int mode, int out, int nwarps,
-                        int grid, cudaStream_t st) {
-    if (group == 32) return has_min ? launch_gemv_g32_m1(p, act, mode, out, nwarps, grid, st)
-                                    : launch_gemv_g32_m0(p, act, mode, out, nwarps, grid, st);
-    return has_min ? launch_gemv_g128_m1(p, act, mode, out, nwarps, grid, st)
-                   : launch_gemv_g128_m0(p, act, mode, out, nwarps, grid, st);
+w4a8_status launch_gemv_mma(const GemvParams& g, bool has_min, int mode, int out, cudaStream_t st);
+w4a8_status device_error(unsigned int* code, cudaStream_t st);
+
+// Group-128 weights with per-token activations go to the tensor-core GEMV;
+// everything else (the engine's group-32 format, per-32 activations) to the dp4a one.
+w4a8_status launch_gemv(const GemvParams& p, int group, bool has_min, int act, int mode, int out, cudaStream_t st) {
+    if (group == 128 && (act == W4A8_ACT_TOKEN || out == OUT_DOTS) && g_use_mma)
+        return launch_gemv_mma(p, has_min, mode, out, st);
+    if (group == 32) return has_min ? launch_gemv_g32_m1(p, act, mode, out, st) : launch_gemv_g32_m0(p, act, mode, out, st);
+    return has_min ? launch_gemv_g128_m1(p, act, mode, out, st) : launch_gemv_g128_m0(p, act, mode, out, st);
 }
 
 namespace {
@@ -71,7 +78,7 @@ w4a8_status check_weight(const w4a8_weight* w, const char* what) {
         return set_error(W4A8_EINVAL, "%s: k=%d is not a positive multiple of group %d", what, w->k, w->group);
     if (w->n <= 0) return set_error(W4A8_EINVAL, "%s: n=%d", what, w->n);
     if (!aligned(w->q, 16)) return set_error(W4A8_EINVAL, "%s: q not 16-byte aligned", what);
-    if (!aligned(w->s, w->has_min ? 4 : 2)) return set_error(W4A8_EINVAL, "%s: s misaligned", what);
+    if (!aligned(w->s, 4)) return set_error(W4A8_EINVAL, "%s: s not 4-byte aligned", what);
     return W4A8_OK;
 }
 
@@ -82,20 +89,6 @@ w4a8_status check_act(const int8_t* xq, const float* xs, int act, const char* wh
     if (!aligned(xq, 16)) return set_error(W4A8_EINVAL, "%s: xq not 16-byte aligned", what);
     if (!aligned(xs, act == W4A8_ACT_GROUP32 ? 8 : 4)) return set_error(W4A8_EINVAL, "%s: xs misaligned", what);
     return W4A8_OK;
-}
-
-// Launch shape of the GEMV family: lanes per row so every lane owns about 8
-// 16-byte chunks of its row, then as many warps per CTA (up to 8) as keep at
-// least two CTAs per SM.
-void gemv_shape(int n_out, int k, int* lpr, int* nwarps, int* grid) {
-    const int kc = k / 32;
-    *lpr = kc >= 192 ? 32 : (kc >= 96 ? 16 : 8);
-    const int rgw = 32 / *lpr;
-    const int target = 2 * sm_count();
-    int nw = kGemvMaxWarps;
-    while (nw > 1 && (n_out + nw * rgw - 1) / (nw * rgw) < target) nw >>= 1;
-    *nwarps = nw;
-    *grid = (n_out + nw * rgw - 1) / (nw * rgw);
 }
 
 }  // namespace
@@ -110,6 +103,12 @@ const char* w4a8_last_error(void) { return t_err; }
 const char* w4a8_version(void) { return "webyiq-b200 w4a8 0.1 (sm_100a)"; }
 
 void w4a8_set_pdl(int enable) { g_use_pdl = enable ? 1 : 0; }
+
+void w4a8_set_gemv_kernel(int tensor_core) { g_use_mma = tensor_core ? 1 : 0; }
+
+w4a8_status w4a8_device_error(uint32_t* code, void* stream) {
+    return device_error(code, static_cast<cudaStream_t>(stream));
+}
 
 w4a8_status w4a8_weight_view(const void* q, const void* s, int32_t n, int32_t k, int32_t group, int32_t has_min,
                              w4a8_weight* out) {
@@ -148,11 +147,10 @@ w4a8_status w4a8_gemv(const w4a8_weight* w, const int8_t* xq, const float* xs, i
     p.xs = xs;
     p.y = y;
     p.n_out = mode == W4A8_SWIGLU ? w->n / 2 : w->n;
+    p.y_stride = p.n_out;
     p.k = w->k;
     p.m = m;
-    int nwarps, grid;
-    gemv_shape(p.n_out, p.k, &p.lpr, &nwarps, &grid);
-    return launch_gemv(p, w->group, w->has_min != 0, act, mode, OUT_Y, nwarps, grid, static_cast<cudaStream_t>(stream));
+    return launch_gemv(p, w->group, w->has_min != 0, act, mode, OUT_Y, static_cast<cudaStream_t>(stream));
 }
 
 w4a8_status w4a8_group_dots(const w4a8_weight* w, const int8_t* xq, int32_t m, int32_t* dots, void* stream) {
@@ -166,11 +164,10 @@ w4a8_status w4a8_group_dots(const w4a8_weight* w, const int8_t* xq, int32_t m, i
     p.xq = xq;
     p.dots = dots;
     p.n_out = w->n;
+    p.y_stride = w->n;
     p.k = w->k;
     p.m = m;
-    int nwarps, grid;
-    gemv_shape(p.n_out, p.k, &p.lpr, &nwarps, &grid);
-    return launch_gemv(p, w->group, w->has_min != 0, W4A8_ACT_TOKEN, W4A8_STORE, OUT_DOTS, nwarps, grid,
+    return launch_gemv(p, w->group, w->has_min != 0, W4A8_ACT_TOKEN, W4A8_STORE, OUT_DOTS,
                        static_cast<cudaStream_t>(stream));
 }
 
@@ -237,13 +234,11 @@ w4a8_status w4a8_lmhead_argmax(const w4a8_weight* w, int32_t row_offset, const i
     p.tok_out = tok_out;
     p.ids = ids;
     p.n_out = w->n;
+    p.y_stride = w->n;
     p.k = w->k;
     p.m = m;
     p.row_offset = row_offset;
-    int nwarps, grid;
-    gemv_shape(p.n_out, p.k, &p.lpr, &nwarps, &grid);
-    return launch_gemv(p, w->group, w->has_min != 0, act, W4A8_STORE, OUT_ARGMAX, nwarps, grid,
-                       static_cast<cudaStream_t>(stream));
+    return launch_gemv(p, w->group, w->has_min != 0, act, W4A8_STORE, OUT_ARGMAX, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -6,7 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/w4a8.h"
+#include "w4a8.h"
 
 namespace w4a8 {
 
@@ -31,11 +31,10 @@ __device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) {
 }
 
 // Dot product of the 32 weights of one 16-byte chunk (4 words) with 32 int8
-// activations (8 words xa, xb): the same term order as gdot (gemv_q4q8.wgsl:29-34),
-// although any order gives the same int32.
+// activations (8 words xa, xb), added to d: the same term order as gdot
+// (gemv_q4q8.wgsl:29-34), although any order gives the same int32.
 __device__ __forceinline__ int chunk_dot(const uint32_t lo[4], const uint32_t hi[4], const uint4& xa,
-                                         const uint4& xb) {
-    int d = 0;
+                                         const uint4& xb, int d) {
     d = dp4a(lo[0], xa.x, d);
     d = dp4a(hi[0], xa.y, d);
     d = dp4a(lo[1], xa.z, d);

@@ -1,0 +1,107 @@
+// Instantiation and launch of the tensor-core GEMV (group 128, per-token int8).
+#include "gemv_mma.cuh"
+#include "launch.cuh"
+
+namespace w4a8 {
+
+int sm_count();  // capi.cu
+
+namespace {
+
+// One CTA per SM (fewer when rows are scarce) on balanced row ranges; a round is
+// RT tiles of 16 rows (8 output rows for SWIGLU); RT x KS warps, KS = ceil(KG/4).
+template <bool HAS_MIN, int MODE, int OUT, int MT>
+w4a8_status launch_mt(MmaParams p, cudaStream_t st) {
+    static size_t configured = 48 * 1024;
+    auto kernel = gemv_mma_kernel<HAS_MIN, MODE, OUT, MT>;
+    const int kg = p.k / 128;
+    p.ks = (kg + kMmaGPS - 1) / kMmaGPS;
+    if (p.ks > kMmaMaxWarps) return set_error(W4A8_EINVAL, "w4a8 gemv: k=%d too large", p.k);
+    const int tr = MODE == W4A8_SWIGLU ? 8 : 16;
+    const int sms = sm_count();
+    int ctas = (p.n_out + 7) / 8;
+    if (ctas > sms) ctas = sms;
+    if (ctas < 1) ctas = 1;
+    const int rows = (p.n_out + ctas - 1) / ctas;
+    int rt = (rows + tr - 1) / tr;
+    const int rt_max = kMmaMaxWarps / p.ks;
+    if (rt > rt_max) rt = rt_max;
+    p.rt = rt < 1 ? 1 : rt;
+    const int rounds = (rows + p.rt * tr - 1) / (p.rt * tr);
+    p.stages = rounds < kMmaMaxStages ? rounds : kMmaMaxStages;
+    const int sb = HAS_MIN ? 4 : 2;
+    MmaSmem plan = mma_smem_plan(p.m, p.k, p.rt, p.ks, p.stages, sb);
+    while (plan.total > 227 * 1024 && p.stages > 1) plan = mma_smem_plan(p.m, p.k, p.rt, p.ks, --p.stages, sb);
+    while (plan.total > 227 * 1024 && p.rt > 1) plan = mma_smem_plan(p.m, p.k, --p.rt, p.ks, p.stages, sb);
+    if (plan.total > 227 * 1024) return set_error(W4A8_EINVAL, "w4a8 gemv: shared memory plan too large");
+    if (plan.total > configured) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan.total));
+        if (e != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8 gemv: smem attribute: %s", cudaGetErrorString(e));
+        configured = plan.total;
+    }
+    return launch_pdl("w4a8 gemv (mma)", kernel, dim3(ctas), dim3(p.rt * p.ks * 32), plan.total, st, p);
+}
+
+template <bool HAS_MIN, int MODE, int OUT>
+w4a8_status launch_one(const MmaParams& p, cudaStream_t st) {
+    if (p.m <= 1) return launch_mt<HAS_MIN, MODE, OUT, 1>(p, st);
+    if (p.m <= 2) return launch_mt<HAS_MIN, MODE, OUT, 2>(p, st);
+    if (p.m <= 4) return launch_mt<HAS_MIN, MODE, OUT, 4>(p, st);
+    return launch_mt<HAS_MIN, MODE, OUT, 8>(p, st);
+}
+
+template <bool HAS_MIN>
+w4a8_status launch_mode(const MmaParams& p, int mode, int out, cudaStream_t st) {
+    if (out == OUT_DOTS) return launch_one<HAS_MIN, W4A8_STORE, OUT_DOTS>(p, st);
+    if (out == OUT_ARGMAX) return launch_one<HAS_MIN, W4A8_STORE, OUT_ARGMAX>(p, st);
+    if (mode == W4A8_STORE) return launch_one<HAS_MIN, W4A8_STORE, OUT_Y>(p, st);
+    if (mode == W4A8_ADD) return launch_one<HAS_MIN, W4A8_ADD, OUT_Y>(p, st);
+    return launch_one<HAS_MIN, W4A8_SWIGLU, OUT_Y>(p, st);
+}
+
+}  // namespace
+
+// GemvParams -> tensor-core launches in token blocks of 8.
+w4a8_status launch_gemv_mma(const GemvParams& g, bool has_min, int mode, int out, cudaStream_t st) {
+    const int kg = g.k / 128;
+    for (int t0 = 0; t0 < g.m; t0 += kMmaTokens) {
+        MmaParams p{};
+        p.q = g.q;
+        p.s = g.s;
+        p.m = g.m - t0 < kMmaTokens ? g.m - t0 : kMmaTokens;
+        p.xq = g.xq + static_cast<size_t>(t0) * g.k;
+        p.xs = g.xs ? g.xs + t0 : nullptr;
+        p.y = g.y ? g.y + static_cast<size_t>(t0) * g.y_stride : nullptr;
+        p.dots = g.dots ? g.dots + static_cast<size_t>(t0) * g.n_out * kg : nullptr;
+        p.counter = g.counter;
+        p.ws_best = g.ws_best ? g.ws_best + t0 : nullptr;
+        p.best_key = g.best_key ? g.best_key + t0 : nullptr;
+        p.tok_out = g.tok_out ? g.tok_out + t0 : nullptr;
+        p.ids = g.ids;
+        p.n_out = g.n_out;
+        p.k = g.k;
+        p.y_stride = g.y_stride;
+        p.row_offset = g.row_offset;
+        const w4a8_status s = has_min ? launch_mode<true>(p, mode, out, st) : launch_mode<false>(p, mode, out, st);
+        if (s != W4A8_OK) return s;
+    }
+    return W4A8_OK;
+}
+
+w4a8_status device_error(unsigned int* code, cudaStream_t st) {
+    unsigned int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_w4a8_dev_error, sizeof(v), 0, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8_device_error: %s", cudaGetErrorString(e));
+    if (v) {
+        const unsigned int zero = 0;
+        e = cudaMemcpyToSymbolAsync(g_w4a8_dev_error, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8_device_error: %s", cudaGetErrorString(e));
+    }
+    if (code) *code = v;
+    return v ? set_error(W4A8_ETIMEOUT, "a bounded device-side wait gave up (code 0x%x)", v) : W4A8_OK;
+}
+
+}  // namespace w4a8

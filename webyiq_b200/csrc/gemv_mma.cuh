@@ -1,0 +1,462 @@
+// W4A8 GEMV on the warp-level integer tensor cores (mma.sync m16n8k32, u8 x s8),
+// for group-128 weights with per-token int8 activations: y = W x for up to 8
+// tokens per launch, the group-dot test hook and the lm_head GEMV with fused
+// argmax.
+//
+// Why this shape (B200 view).  The GEMV streams packed weights from HBM once; the
+// SM must turn every 16 weight bytes into dot products with as few instructions
+// and as short dependency chains as possible, so that the post-wait critical
+// path (activations in, math, outputs out) is short.  The packed words go into
+// the tensor core unchanged:
+//  - A packed word i holds weights 8i..8i+3 in its low nibbles and 8i+4..8i+7 in
+//    its high nibbles (tools/convert.py:7-11).  w & 0x0F0F0F0F is the first four
+//    as u8 bytes; w & 0xF0F0F0F0 is the other four times 16, still u8.  Each goes
+//    into the tensor core against the raw int8 activation word it meets, in two
+//    accumulators, and the exact int32 group dot is D_lo + (D_hi16 >> 4).  (The
+//    int4 mma forms would take the packed words as they are, but they run far
+//    slower than the int8 form on sm_100.)
+//  - A = 16 weight rows x 32 k, B = 32 k x 8 tokens.  Lane (g, t) = (lane/4,
+//    lane%4) loads 16 contiguous bytes (k-words 4t..4t+3 of a 128-group) of rows g
+//    and g+8; per group that is two low-nibble and two high-nibble mma.  The D
+//    fragment holds the group dots of rows g, g+8 for tokens 2t, 2t+1, and the
+//    exact per-group scale step runs in the lanes that own those rows.
+//  - A CTA (one per SM, persistent) owns a balanced contiguous row range, walked
+//    in rounds of RT 16-row tiles; its warps are RT x KS (tile, K-slice) tasks of
+//    up to 4 groups, so every lane holds at most 8 x 16 weight bytes, requested
+//    before griddepcontrol.wait.  K-slice partial sums meet in shared memory and
+//    are added in slice order (int64: exact anyway).
+//
+// Reference: gemv_q4q8.wgsl:36-131 (per-group math at :68, modes at :122-129),
+// argmax.wgsl:14-43 for the fused argmax.  Numerics: the exact per-token path of
+// w4a8.h, y = ((float)(sum_g fix(s)*(I - 8X) [+ fix(min)*X]) * 2^-24) * dx.
+#pragma once
+
+#include "gemv.cuh"
+
+namespace w4a8 {
+
+constexpr int kMmaMaxWarps = 16;
+constexpr int kMmaGPS = 4;      // groups per K-slice task
+constexpr int kMmaTokens = 8;   // tokens per launch (the mma N)
+constexpr int kMmaMaxStages = 3;
+constexpr long long kWaitLimitCycles = 1ll << 29;  // bounded waits: ~0.3 s at 2 GHz
+
+// Set (atomicOr) by a kernel whose bounded wait gave up; read and cleared by
+// w4a8_device_error.  Defined here: only gemv_mma.cu includes this header.
+__device__ unsigned int g_w4a8_dev_error = 0;
+enum : unsigned int { DEV_ERR_TMA_TIMEOUT = 1u };
+
+struct MmaParams {
+    const uint4* q;        // [rows, k/32] 16-byte chunks
+    const void* s;         // scales: u16 f16 (symmetric) or u32 (scale, min)
+    const int8_t* xq;      // [m, k]
+    const float* xs;       // [m] per-token dx
+    float* y;              // OUT_Y output; OUT_ARGMAX logits or null
+    int* dots;             // OUT_DOTS [m, n_out, k/128]
+    unsigned int* counter;
+    unsigned long long* ws_best;
+    unsigned long long* best_key;
+    unsigned int* tok_out;
+    const unsigned int* ids;
+    int n_out;      // output rows
+    int k;
+    int m;          // tokens (<= 8)
+    int y_stride;
+    int row_offset;
+    int rt;         // tiles per round
+    int ks;         // K-slices
+    int stages;     // weight stages in shared memory
+};
+
+// Padded shared-memory row stride for k/2 weight bytes: stride = 80 (mod 128) makes
+// the 32 lanes' 16-byte A-operand reads (rows gq, columns tq) hit every bank
+// exactly 4 times, the minimum for 512 bytes.
+__host__ __device__ inline int mma_row_stride(int k) {
+    const int b = k / 2;
+    return b + ((80 - b % 128) % 128 + 128) % 128;
+}
+
+// Shared memory: weight stages [S][rt*16 rows][stride], their scales
+// [S][rt*16 rows][k/128] (rows in the order they are copied), activation operands
+// [KG][m][4][8 words] (the 32 bytes lane-quarter t meets), per-group activation
+// sums [KG][m], K-slice partial sums [rt][ks][16][8] (int64), one mbarrier per stage.
+struct MmaSmem {
+    size_t stage, stage_bytes, sc, sc_bytes, xf, xg, dx, red, bar, total;
+};
+__host__ __device__ inline MmaSmem mma_smem_plan(int m, int k, int rt, int ks, int stages, int sb) {
+    MmaSmem s{};
+    const size_t kg = static_cast<size_t>(k) / 128;
+    auto up = [](size_t v) { return (v + 127) & ~static_cast<size_t>(127); };
+    s.stage = 0;
+    s.stage_bytes = static_cast<size_t>(rt) * 16 * mma_row_stride(k);
+    s.sc = up(s.stage + stages * s.stage_bytes);        // scales [S][rt*16 rows][kg] (gate | up)
+    s.sc_bytes = up(static_cast<size_t>(rt) * 16 * kg * sb);
+    s.xf = up(s.sc + stages * s.sc_bytes);
+    s.xg = s.xf + kg * m * 4 * 32;
+    s.dx = up(s.xg + kg * m * 4);                       // per-token dx [8]
+    s.red = up(s.dx + kMmaTokens * 4);
+    s.bar = up(s.red + static_cast<size_t>(rt) * ks * 16 * kMmaTokens * 8);
+    s.total = s.bar + kMmaMaxStages * 8;
+    return s;
+}
+
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// --- TMA bulk copies and mbarriers (no cluster multicast anywhere) -----------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// Orders this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (TMA) accesses.
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tma_bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+// Wait for phase `parity` of the barrier, giving up after kWaitLimitCycles.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    const long long t0 = clock64();
+    while (true) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (clock64() - t0 > kWaitLimitCycles) return false;
+    }
+}
+
+// One token: 64 registers, so the next kernel's CTA fits beside this one and its
+// TMA copies start while this one finishes.  More tokens: room for the epilogue.
+template <int MT>
+struct MmaBounds {
+    static constexpr int min_blocks = MT == 1 ? 2 : 1;
+};
+
+template <bool HAS_MIN, int MODE, int OUT, int MT>
+__global__ void __launch_bounds__(kMmaMaxWarps * 32, MmaBounds<MT>::min_blocks)
+gemv_mma_kernel(const MmaParams p) {
+    constexpr bool SWI = (MODE == W4A8_SWIGLU);
+    constexpr int TR = SWI ? 8 : 16;  // output rows per tile
+    extern __shared__ __align__(128) unsigned char smem[];
+
+    const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int gq = lane >> 2, tq = lane & 3;  // mma group / thread-in-group
+    const int KC = p.k >> 5, KG = p.k >> 7;
+    const int m = MT < p.m ? MT : p.m;  // MT: compile-time bound on the tokens
+    const int rt = p.rt, ks = p.ks, S = p.stages;
+    const int tile = warp / ks, slice = warp - tile * ks;  // this warp's task
+    const bool active = tile < rt;
+    const int g0 = static_cast<int>(static_cast<long long>(slice) * KG / ks);
+    const int g1 = static_cast<int>(static_cast<long long>(slice + 1) * KG / ks);
+    const int ng = g1 - g0;  // <= kMmaGPS (host guarantees)
+    const int stride = mma_row_stride(p.k);
+    const int sb = HAS_MIN ? 4 : 2;
+    const MmaSmem sp = mma_smem_plan(m, p.k, rt, ks, S, sb);
+    // scales travel with the weights when a row of them is a whole number of
+    // 16-byte units (k % 1024 == 0 symmetric, k % 512 == 0 with mins)
+    const bool scale_tma = ((KG * sb) & 15) == 0;
+    float* sdx = reinterpret_cast<float*>(smem + sp.dx);
+    uint32_t* xf = reinterpret_cast<uint32_t*>(smem + sp.xf);
+    int* xg = reinterpret_cast<int*>(smem + sp.xg);
+    long long* red = reinterpret_cast<long long*>(smem + sp.red);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + sp.bar);
+
+    const int rb = static_cast<int>(static_cast<long long>(blockIdx.x) * p.n_out / gridDim.x);
+    const int re = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * p.n_out / gridDim.x);
+    const int rows_round = rt * TR;
+    const int rounds = (re - rb + rows_round - 1) / rows_round;
+
+    // Warp 0 requests round r into stage `slot`: one bulk copy per weight row into
+    // its padded shared-memory row (A rows 0-7 gate / 8-15 up for SWIGLU).
+    auto issue = [&](int r, int slot) {
+        const int o0 = rb + r * rows_round;
+        const int nrow = min(rows_round, re - o0);
+        const int ncopy = (SWI ? 2 : 1) * nrow;
+        const uint32_t row_bytes = static_cast<uint32_t>(p.k / 2);
+        const uint32_t srow_bytes = static_cast<uint32_t>(KG * sb);
+        if (lane == 0) {
+            mbar_expect_tx(&bar[slot], static_cast<uint32_t>(ncopy) * (row_bytes + (scale_tma ? srow_bytes : 0u)));
+            if (scale_tma) {  // [h][row][KG]: gate (or all) rows, then up rows
+                unsigned char* sdst = smem + sp.sc + static_cast<size_t>(slot) * sp.sc_bytes;
+                for (int h = 0; h < (SWI ? 2 : 1); ++h)
+                    tma_bulk_load(sdst + static_cast<size_t>(h) * rows_round * srow_bytes,
+                                  static_cast<const unsigned char*>(p.s) +
+                                      (static_cast<size_t>(o0) + static_cast<size_t>(h) * p.n_out) * srow_bytes,
+                                  static_cast<uint32_t>(nrow) * srow_bytes, &bar[slot]);
+            }
+        }
+        __syncwarp();
+        unsigned char* st = smem + sp.stage + static_cast<size_t>(slot) * sp.stage_bytes;
+        for (int i = lane; i < ncopy; i += 32) {
+            const int h = SWI ? (i >= nrow) : 0;
+            const int ri = i - h * nrow;
+            const int srow = SWI ? (ri / 8) * 16 + (ri % 8) + 8 * h : ri;
+            const uint4* src = p.q + (static_cast<size_t>(o0 + ri) + static_cast<size_t>(h) * p.n_out) * KC;
+            tma_bulk_load(st + static_cast<size_t>(srow) * stride, src, row_bytes, &bar[slot]);
+        }
+    };
+    auto prefetch_scales = [&](int r) {  // the fallback: the round's scale span towards L2
+        if (scale_tma || tid != 0 || r >= rounds) return;
+        const int o0 = rb + r * rows_round, o1 = min(o0 + rows_round, re);
+        const size_t sb = HAS_MIN ? 4 : 2;
+        for (int h = 0; h < (SWI ? 2 : 1); ++h) {
+            const size_t r0 = static_cast<size_t>(o0) + static_cast<size_t>(h) * p.n_out;
+            const size_t b0 = r0 * KG * sb, b1 = (r0 + (o1 - o0)) * KG * sb;
+            const size_t a0 = (b0 + 15) & ~static_cast<size_t>(15), a1 = b1 & ~static_cast<size_t>(15);
+            if (a1 > a0) l2_prefetch_bulk(static_cast<const unsigned char*>(p.s) + a0, static_cast<uint32_t>(a1 - a0));
+        }
+    };
+    // stored rows behind A rows gq and gq+8 of this warp's tile in round r
+    auto lane_rows = [&](int r, int& ra, int& rc, bool& oka, bool& okc) {
+        const int t0 = rb + r * rows_round + tile * TR;
+        ra = t0 + gq;
+        rc = SWI ? t0 + gq + p.n_out : t0 + gq + 8;
+        oka = active && t0 + gq < re;
+        okc = active && (SWI ? t0 + gq < re : t0 + gq + 8 < re);
+    };
+    uint32_t sa[kMmaGPS], sc[kMmaGPS];
+    auto load_scales = [&](int r) {  // the fallback when scales are not staged by TMA
+        if (scale_tma) return;
+        int ra, rc;
+        bool oka, okc;
+        lane_rows(r, ra, rc, oka, okc);
+#pragma unroll
+        for (int j = 0; j < kMmaGPS; ++j) {
+            const size_t ea = static_cast<size_t>(ra) * KG + g0 + j, ec = static_cast<size_t>(rc) * KG + g0 + j;
+            sa[j] = sc[j] = 0u;
+            if (j < ng && oka)
+                sa[j] = HAS_MIN ? __ldg(static_cast<const uint32_t*>(p.s) + ea)
+                                : static_cast<uint32_t>(__ldg(static_cast<const unsigned short*>(p.s) + ea));
+            if (j < ng && okc)
+                sc[j] = HAS_MIN ? __ldg(static_cast<const uint32_t*>(p.s) + ec)
+                                : static_cast<uint32_t>(__ldg(static_cast<const unsigned short*>(p.s) + ec));
+        }
+    };
+
+    // Weights first: they do not depend on the previous kernel.
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int s2 = 0; s2 < S; ++s2) mbar_init(&bar[s2], 1);
+            mbar_init_fence();
+        }
+        __syncwarp();
+        for (int r = 0; r < S && r < rounds; ++r) issue(r, r);
+    }
+    prefetch_scales(0);
+    prefetch_scales(1);
+    pdl_launch_dependents();
+    pdl_wait();  // activations (and y for ADD) come from the previous kernel
+
+    load_scales(0);
+    if (OUT != OUT_DOTS && tid < m) sdx[tid] = __ldg(p.xs + tid);  // the dots hook has no xs
+    // Activation operands and group sums.  Work item (g, t, tq): the 32 bytes
+    // x[t][128g + 32tq ..] that lane-quarter tq of the mma meets, stored as
+    // [g][t][tq][8 words]; the quarter sums of a group are added by shuffles
+    // (items of one (g, t) are 4 neighbouring threads).
+    {
+        const int nitem = KG * m * 4;
+        for (int i0 = 0; i0 < nitem; i0 += blockDim.x) {
+            const int i = i0 + tid;
+            int X = 0;
+            if (i < nitem) {
+                const int tq2 = i & 3, t = (i >> 2) % m, g = (i >> 2) / m;
+                const uint4* src = reinterpret_cast<const uint4*>(p.xq + static_cast<size_t>(t) * p.k + g * 128 + tq2 * 32);
+                const uint4 u = __ldg(src), v = __ldg(src + 1);
+                uint4* dst = reinterpret_cast<uint4*>(xf + static_cast<size_t>(i) * 8);
+                dst[0] = u;
+                dst[1] = v;
+                X = chunk_sum(u, v);
+            }
+            X += __shfl_xor_sync(kFull, X, 1);
+            X += __shfl_xor_sync(kFull, X, 2);
+            if (i < nitem && (i & 3) == 0) xg[i >> 2] = X;  // [g][t]
+        }
+    }
+    __syncthreads();
+
+    unsigned long long best[MT];  // OUT_ARGMAX: running best key per token (finalizing threads)
+#pragma unroll
+    for (int t = 0; t < MT; ++t) best[t] = 0ull;
+
+    for (int r = 0; r < rounds; ++r) {
+        const int slot = r % S;
+        const bool ok_wait = mbar_wait(&bar[slot], static_cast<uint32_t>((r / S) & 1));
+        if (__syncthreads_or(!ok_wait)) {  // a copy never landed: report, do not hang
+            if (tid == 0) atomicOr(&g_w4a8_dev_error, DEV_ERR_TMA_TIMEOUT);
+            return;
+        }
+        prefetch_scales(r + 2);
+        int ra, rc;
+        bool oka, okc;
+        lane_rows(r, ra, rc, oka, okc);
+        const unsigned char* st = smem + sp.stage + static_cast<size_t>(slot) * sp.stage_bytes;
+        const unsigned char* scs = smem + sp.sc + static_cast<size_t>(slot) * sp.sc_bytes;
+        // staged scale rows of A rows gq and gq+8 (index [h][row in round][g])
+        const int ria = SWI ? tile * TR + gq : tile * 16 + gq;
+        const int ric = SWI ? rows_round + ria : ria + 8;
+        const unsigned char* rowa = st + static_cast<size_t>(tile * 16 + gq) * stride + tq * 16;
+        const unsigned char* rowc = rowa + static_cast<size_t>(8) * stride;
+        long long acc[4] = {0, 0, 0, 0};  // [row gq | gq+8][token 2tq | 2tq+1]
+#pragma unroll
+        for (int j = 0; j < kMmaGPS; ++j) {
+            if (j >= ng) break;
+            const int g = g0 + j;
+            uint4 wa = make_uint4(0, 0, 0, 0), wc = make_uint4(0, 0, 0, 0);
+            if (active) {
+                wa = *reinterpret_cast<const uint4*>(rowa + g * 64);
+                wc = *reinterpret_cast<const uint4*>(rowc + g * 64);
+            }
+            uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
+            if (gq < m) {  // B column gq = token gq (lanes 4t..4t+3)
+                const uint4* xp = reinterpret_cast<const uint4*>(xf + ((static_cast<size_t>(g) * m + gq) * 4 + tq) * 8);
+                x0 = xp[0];  // activations of k-words 0, 1 (low 4, high 4 each)
+                x1 = xp[1];  // k-words 2, 3
+            }
+            const uint32_t ml = 0x0F0F0F0Fu, mh = 0xF0F0F0F0u;
+            int dl[4] = {0, 0, 0, 0}, dh[4] = {0, 0, 0, 0};
+            // k-words w0, w1 of rows gq (wa) and gq+8 (wc); A k-slots 0-3 / 16-19
+            // of this lane meet B words 0 / 1 of the same lane
+            mma_u8s8(dl, wa.x & ml, wc.x & ml, wa.y & ml, wc.y & ml, x0.x, x0.z);
+            mma_u8s8(dl, wa.z & ml, wc.z & ml, wa.w & ml, wc.w & ml, x1.x, x1.z);
+            mma_u8s8(dh, wa.x & mh, wc.x & mh, wa.y & mh, wc.y & mh, x0.y, x0.w);
+            mma_u8s8(dh, wa.z & mh, wc.z & mh, wa.w & mh, wc.w & mh, x1.y, x1.w);
+            // element e: A row gq (e < 2) or gq+8, token 2tq + (e & 1)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int t = 2 * tq + (e & 1);
+                if ((e & 1) >= MT || t >= m) continue;
+                const int I = dl[e] + (dh[e] >> 4);  // dh = 16 * high-nibble dot, exact
+                const int X = xg[g * m + t];
+                uint32_t s;
+                if (scale_tma) {
+                    const size_t si = static_cast<size_t>(e < 2 ? ria : ric) * KG + g;
+                    s = HAS_MIN ? reinterpret_cast<const uint32_t*>(scs)[si]
+                                : static_cast<uint32_t>(reinterpret_cast<const unsigned short*>(scs)[si]);
+                } else {
+                    s = e < 2 ? sa[j] : sc[j];
+                }
+                if (OUT == OUT_DOTS) {
+                    const bool ok = e < 2 ? oka : okc;
+                    const int row = e < 2 ? ra : rc;
+                    if (ok) p.dots[(static_cast<size_t>(t) * p.n_out + row) * KG + g] = HAS_MIN ? I : I - 8 * X;
+                } else if (HAS_MIN) {
+                    const Fix16 fs = fix16(s & 0xffffu), fm = fix16(s >> 16);
+                    acc[e] += shl64(fs.mant * I, fs.sh) + shl64(fm.mant * X, fm.sh);
+                } else {
+                    const Fix16 fs = fix16(s);
+                    acc[e] += shl64(fs.mant * (I - 8 * X), fs.sh);
+                }
+            }
+        }
+        if (r + 1 < rounds) load_scales(r + 1);  // in flight during the sums below
+        if (OUT != OUT_DOTS && active) {  // K-slice partial sums: red[tile][slice][A row][token]
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int t = 2 * tq + (e & 1);
+                const int arow = gq + (e >= 2 ? 8 : 0);
+                if ((e & 1) < MT && t < m) red[((static_cast<size_t>(tile) * ks + slice) * 16 + arow) * kMmaTokens + t] = acc[e];
+            }
+        }
+        __syncthreads();  // every warp is done with stage `slot` and has stored its sums
+        if (warp == 0 && r + S < rounds) {
+            fence_proxy_async();
+            issue(r + S, slot);
+        }
+        if (OUT == OUT_DOTS) continue;
+        // one thread per (output row, token): add the slices in order
+        const int nout = min(rows_round, re - (rb + r * rows_round));
+        for (int i = tid; i < nout * m; i += blockDim.x) {
+            const int t = i % m, orow = i / m;  // output row within the round
+            const int tl = orow / TR, rw = orow - tl * TR;
+            long long a0 = 0, a1 = 0;
+            for (int s2 = 0; s2 < ks; ++s2) {
+                a0 += red[((static_cast<size_t>(tl) * ks + s2) * 16 + rw) * kMmaTokens + t];
+                if (SWI) a1 += red[((static_cast<size_t>(tl) * ks + s2) * 16 + rw + 8) * kMmaTokens + t];
+            }
+            const float dx = sdx[t];
+            const float v0 = fix_to_float(a0, dx);
+            const int row = rb + r * rows_round + orow;
+            if (OUT == OUT_Y) {
+                float* yp = p.y + static_cast<size_t>(t) * p.y_stride + row;
+                if (MODE == W4A8_STORE)
+                    *yp = v0;
+                else if (MODE == W4A8_ADD)
+                    *yp = __fadd_rn(*yp, v0);
+                else
+                    *yp = silu_mul(v0, fix_to_float(a1, dx));
+            } else {
+                if (p.y != nullptr) p.y[static_cast<size_t>(t) * p.y_stride + row] = v0;
+                const unsigned long long key = argmax_key(v0, static_cast<uint32_t>(p.row_offset + row));
+#pragma unroll
+                for (int tt = 0; tt < MT; ++tt)
+                    if (tt == t) best[tt] = key > best[tt] ? key : best[tt];
+            }
+        }
+        __syncthreads();  // `red` is rewritten by the next round
+    }
+
+    if (OUT != OUT_ARGMAX) return;
+
+    // Max per token over the CTA, one atomicMax per token, and the last CTA to
+    // finish publishes the result and re-zeroes the workspace.
+    __shared__ unsigned long long s_key[kMmaMaxWarps][MT];
+    __shared__ bool s_last;
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+        unsigned long long key = best[t];
+        for (int off = 1; off < 32; off <<= 1) {
+            const unsigned long long o = shfl_xor_u64(key, off);
+            key = o > key ? o : key;
+        }
+        if (lane == 0) s_key[warp][t] = key;
+    }
+    __syncthreads();
+    if (tid < m) {
+        unsigned long long key = 0;
+        for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) key = s_key[w][tid] > key ? s_key[w][tid] : key;
+        if (key) atomicMax(p.ws_best + tid, key);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned int done = atomicAdd(p.counter, 1u);
+        s_last = (done == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (s_last) {
+        __threadfence();
+        if (tid < m) {
+            const unsigned long long key = atomicExch(p.ws_best + tid, 0ull);
+            p.best_key[tid] = key;
+            if (p.tok_out) {
+                const uint32_t idx = key ? ~static_cast<uint32_t>(key & 0xffffffffu) : 0u;
+                p.tok_out[tid] = p.ids ? __ldg(p.ids + idx) : idx;
+            }
+        }
+        if (tid == 0) *p.counter = 0u;
+    }
+}
+
+}  // namespace w4a8

@@ -152,3 +152,16 @@ def key_index(key):
 
 def set_pdl(enable):
     _lib.load().w4a8_set_pdl(1 if enable else 0)
+
+
+def device_error():
+    """Synchronize the current stream and raise W4A8Error(ETIMEOUT) if a kernel's
+    bounded wait gave up since the last check."""
+    code = ctypes.c_uint32(0)
+    _lib.check(_lib.load().w4a8_device_error(ctypes.byref(code), _stream()))
+    return code.value
+
+
+def set_gemv_kernel(tensor_core):
+    """Group-128 per-token GEMVs on the tensor-core kernel (True) or dp4a (False)."""
+    _lib.load().w4a8_set_gemv_kernel(1 if tensor_core else 0)
