@@ -145,6 +145,22 @@ W4A8_API w4a8_status w4a8_lmhead_argmax(const w4a8_weight* w, int32_t row_offset
                                void* workspace, size_t workspace_bytes, void* stream);
 W4A8_API size_t w4a8_lmhead_workspace_bytes(int32_t n, int32_t m);
 
+/* w4a8_lmhead_argmax without a workspace and without any device allocation, for
+ * callers that cannot allocate device memory where they sample (a plugin inside an
+ * engine that owns all device memory; a decode loop that must not call cudaMalloc,
+ * which synchronizes the device).  The scratch (CTA-done counter and the running
+ * keys of up to 16 tokens) is a 256-byte array inside this library, one per GPU,
+ * held until the process exits.  m > 16 is rejected with W4A8_EINVAL.  Every call
+ * on a GPU shares that array and leaves it zeroed; calls that overlap on the GPU
+ * race on it.  The first call on a device looks up the array's address and
+ * zero-fills it (cudaGetSymbolAddress, cudaMemset): make that first call outside
+ * any stream capture.  Other arguments as w4a8_lmhead_argmax.
+ * No counterpart in the reference (an addition of this library). */
+W4A8_API w4a8_status w4a8_lmhead_argmax_noalloc(const w4a8_weight* w, int32_t row_offset,
+                                               const int8_t* xq, const float* xs, int32_t act,
+                                               int32_t m, float* logits, uint64_t* best_key,
+                                               uint32_t* tok_out, const uint32_t* ids, void* stream);
+
 /* Index carried by a packed argmax key (0 for the "no value > -3e38" key 0). */
 static inline uint32_t w4a8_key_index(uint64_t key) {
     return key ? ~(uint32_t)(key & 0xffffffffu) : 0u;

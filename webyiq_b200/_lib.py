@@ -41,6 +41,7 @@ _SIGS = {
     "w4a8_lmhead_argmax": (ctypes.c_int, [ctypes.POINTER(Weight), _I, _P, _P, _I, _I, _P, _P, _P, _P, _P,
                                           ctypes.c_size_t, _P]),
     "w4a8_lmhead_workspace_bytes": (ctypes.c_size_t, [_I, _I]),
+    "w4a8_lmhead_argmax_noalloc": (ctypes.c_int, [ctypes.POINTER(Weight), _I, _P, _P, _I, _I, _P, _P, _P, _P, _P]),
     "w4a8_group_dots": (ctypes.c_int, [ctypes.POINTER(Weight), _P, _I, _P, _P]),
     "w4a8_set_pdl": (None, [ctypes.c_int]),
     "w4a8_set_gemv_kernel": (None, [ctypes.c_int]),

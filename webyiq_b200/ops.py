@@ -144,6 +144,21 @@ def lmhead_argmax(w, xq, xs, act=ACT_TOKEN, row_offset=0, logits=None, ids=None,
     return best_key, tok
 
 
+def lmhead_argmax_noalloc(w, xq, xs, act=ACT_TOKEN, row_offset=0, logits=None, ids=None, best_key=None, tok=None):
+    """lm_head GEMV with fused argmax, using the library's own scratch (no workspace,
+    no device allocation; m <= 16).  Returns (best_key int64 [m], tok int32 [m])."""
+    _need_cuda(xq, xs, logits, ids)
+    m = xq.shape[0]
+    dev = xq.device
+    if best_key is None:
+        best_key = torch.empty(m, dtype=torch.int64, device=dev)
+    if tok is None:
+        tok = torch.empty(m, dtype=torch.int32, device=dev)
+    _lib.check(_lib.load().w4a8_lmhead_argmax_noalloc(ctypes.byref(w.c), int(row_offset), _ptr(xq), _ptr(xs), act, m,
+                                                      _ptr(logits), _ptr(best_key), _ptr(tok), _ptr(ids), _stream()))
+    return best_key, tok
+
+
 def key_index(key):
     """Index carried by a packed argmax key (python int, u64 bits)."""
     key &= (1 << 64) - 1
