@@ -394,6 +394,34 @@ def cpu_baseline_sample(seconds=10.0):
 
 
 # ---------------------------------------------------------------------------
+def run_case(case, iters, torch, ops, dev):
+    """A small, fixed workload for profiling one kernel (4 rotating weight copies)."""
+    kind, *dims = case.split(":")
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    k, n = int(dims[0]), int(dims[1])
+    m = int(dims[2]) if len(dims) > 2 else 1
+    ws = [rand_weight(n, k, GROUP, gen, dev, torch, ops) for _ in range(4)]
+    xq, xs = ops.quant(torch.randn((m, k), device=dev, generator=gen), act=ops.ACT_TOKEN)
+    if kind == "gemv":
+        y = torch.empty((m, n), device=dev)
+        for i in range(iters):
+            ops.gemv(ws[i % 4], xq, xs, act=ops.ACT_TOKEN, y=y)
+    elif kind == "lmhead":
+        wsp = ops.lmhead_workspace(ws[0], m, dev)
+        for i in range(iters):
+            ops.lmhead_argmax(ws[i % 4], xq, xs, act=ops.ACT_TOKEN, workspace=wsp)
+    elif kind == "gemm":
+        y = torch.empty((m, n), device=dev)
+        for i in range(iters):
+            ops.gemm(ws[i % 4], xq, xs, act=ops.ACT_TOKEN, y=y)
+    else:
+        raise SystemExit(f"unknown case {case}")
+    torch.cuda.synchronize()
+    ops.device_error()
+    print(f"case {case}: {iters} calls ok")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -402,6 +430,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--case", default=None,
+                    help="profiling case instead of the benchmark: 'gemv:K:N[:M]' or 'lmhead:K:N' runs that "
+                         "call `--steps` times on rotating weights (small, for ncu)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -422,6 +453,9 @@ def main():
     _lib.load()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.case:
+        run_case(args.case, args.steps, torch, ops, dev)
+        return
     dist = None
     if world > 1:
         import datetime

@@ -61,7 +61,8 @@ w4a8_status device_error(unsigned int* code, cudaStream_t st);
 // Group-128 weights with per-token activations go to the tensor-core GEMV;
 // everything else (the engine's group-32 format, per-32 activations) to the dp4a one.
 w4a8_status launch_gemv(const GemvParams& p, int group, bool has_min, int act, int mode, int out, cudaStream_t st) {
-    if (group == 128 && (act == W4A8_ACT_TOKEN || out == OUT_DOTS) && g_use_mma)
+    // (the lm_head argmax stays on the dp4a kernel: measured faster for vocabulary-sized n)
+    if (group == 128 && (act == W4A8_ACT_TOKEN || out == OUT_DOTS) && out != OUT_ARGMAX && g_use_mma)
         return launch_gemv_mma(p, has_min, mode, out, st);
     if (group == 32) return has_min ? launch_gemv_g32_m1(p, act, mode, out, st) : launch_gemv_g32_m0(p, act, mode, out, st);
     return has_min ? launch_gemv_g128_m1(p, act, mode, out, st) : launch_gemv_g128_m0(p, act, mode, out, st);

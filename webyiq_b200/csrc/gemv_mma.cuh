@@ -130,14 +130,22 @@ __device__ __forceinline__ void tma_bulk_load(void* dst, const void* src, uint32
                  ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
-// Wait for phase `parity` of the barrier, giving up after kWaitLimitCycles.
+// Wait for phase `parity` of the barrier, giving up after kWaitLimitCycles: a
+// non-blocking test first (the phase is usually complete by now), then the
+// hardware-suspending try_wait, so a waiting thread does not spin on the issue port.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     const uint32_t a = smem_u32(bar);
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
     const long long t0 = clock64();
     while (true) {
-        uint32_t done;
         asm volatile(
-            "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(done)
             : "r"(a), "r"(parity)
             : "memory");
@@ -302,7 +310,8 @@ gemv_mma_kernel(const MmaParams p) {
 
     for (int r = 0; r < rounds; ++r) {
         const int slot = r % S;
-        const bool ok_wait = mbar_wait(&bar[slot], static_cast<uint32_t>((r / S) & 1));
+        // one thread waits for the copies; the barrier releases (and orders) the rest
+        const bool ok_wait = tid != 0 || mbar_wait(&bar[slot], static_cast<uint32_t>((r / S) & 1));
         if (__syncthreads_or(!ok_wait)) {  // a copy never landed: report, do not hang
             if (tid == 0) atomicOr(&g_w4a8_dev_error, DEV_ERR_TMA_TIMEOUT);
             return;
