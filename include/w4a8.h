@@ -36,8 +36,10 @@
  * scale*I + min*sum(xq) is an integer multiple of 2^-24 (f16 scales are), it is
  * accumulated in int64, and the output is ((float)acc * 2^-24) * dx, rounded twice
  * and independent of how the work was split.  So results are bit-identical across
- * the GEMV, the GEMM, any grid size and any number of GPUs, and the argmax ids are
- * exact.  The accumulator cannot overflow while k * 1905 * (|scale| + |min|) < 2^39
+ * the GEMV kernels, any grid size and any number of GPUs, and the argmax ids are
+ * exact.  The tensor-core GEMM (group 128, symmetric, W4A8_ACT_TOKEN, used by
+ * w4a8_gemm) keeps the int32 group dots exact but does the scale step in f32:
+ * y = (sum_g f32(s) * f32(I)) * dx, within 1e-6 relative of the exact path.  The accumulator cannot overflow while k * 1905 * (|scale| + |min|) < 2^39
  * for every group (for k = 8192: |scale| + |min| < 35000).  With W4A8_ACT_GROUP32 the
  * group terms s*dx*I + m*dxsum are accumulated in f32 (as gemv_q4q8.wgsl:68 does),
  * so results agree with any other order to f32 rounding.
@@ -114,7 +116,10 @@ W4A8_API w4a8_status w4a8_gemv(const w4a8_weight* w, const int8_t* xq, const flo
                       int32_t m, int32_t mode, float* y, void* stream);
 
 /* Prefill GEMM Y[m, n] = X W^T for any m >= 1 (gemm_q4q8.wgsl:46-121,
- * Builder::gemm graph.rs:200-205). */
+ * Builder::gemm graph.rs:200-205).  Group-128 symmetric weights with
+ * W4A8_ACT_TOKEN run on the tcgen05 tensor cores (int4 expanded to int8 in shared
+ * memory, int32 accumulators in tensor memory); other formats run the GEMV kernels
+ * over blocks of W4A8_GEMV_MAX_M tokens. */
 W4A8_API w4a8_status w4a8_gemm(const w4a8_weight* w, const int8_t* xq, const float* xs, int32_t act,
                       int32_t m, int32_t mode, float* y, void* stream);
 
@@ -173,6 +178,12 @@ static inline uint32_t w4a8_key_index(uint64_t key) {
 W4A8_API w4a8_status w4a8_group_dots(const w4a8_weight* w, const int8_t* xq, int32_t m, int32_t* dots,
                             void* stream);
 
+/* Test hook: the int32 group dots of the tensor-core GEMM (same layout and values
+ * as w4a8_group_dots, any m >= 1), read back from its tensor-memory accumulators.
+ * Group-128 symmetric weights only (W4A8_ENOTSUP otherwise). */
+W4A8_API w4a8_status w4a8_gemm_group_dots(const w4a8_weight* w, const int8_t* xq, int32_t m,
+                                          int32_t* dots, void* stream);
+
 /* Tuning: enable (default) or disable programmatic dependent launch, which lets a
  * kernel's CTAs start (and prefetch weights) while the previous kernel in the
  * stream drains.  Process-wide. */
@@ -183,8 +194,12 @@ W4A8_API void w4a8_set_pdl(int enable);
  * Process-wide. */
 W4A8_API void w4a8_set_gemv_kernel(int tensor_core);
 
-/* Device-side error word: every wait inside a kernel (for a TMA copy to land) is
- * bounded; a wait that gives up records a code here and the kernel returns
+/* Tuning / testing: route the GEMM formats the tcgen05 kernel covers to it (1,
+ * default) or to the GEMV kernels over token blocks (0).  Process-wide. */
+W4A8_API void w4a8_set_gemm_kernel(int tensor_core);
+
+/* Device-side error word: every wait inside a kernel (for a TMA copy to land, for
+ * a tensor-core step to finish) is bounded; a wait that gives up records a code here and the kernel returns
  * without touching its outputs.  This call synchronizes `stream`, returns
  * W4A8_ETIMEOUT and the code if any was recorded (and clears it), else W4A8_OK.
  * code may be NULL. */

@@ -13,6 +13,7 @@ namespace w4a8 {
 
 int g_use_pdl = 1;
 int g_use_mma = 1;
+int g_use_tc_gemm = 1;
 
 namespace {
 thread_local char t_err[512] = "";
@@ -57,6 +58,13 @@ w4a8_status launch_argmax(const float*, int, int, const uint32_t*, uint32_t*, cu
 
 w4a8_status launch_gemv_mma(const GemvParams& g, bool has_min, int mode, int out, cudaStream_t st);
 w4a8_status device_error(unsigned int* code, cudaStream_t st);
+w4a8_status launch_gemm_tc(const w4a8_weight* w, const int8_t* xq, const float* dx, int m, int mode, float* y,
+                           int* dots, cudaStream_t st);
+
+// The formats the tcgen05 GEMM covers: group-128 symmetric weights, per-token dx.
+bool tc_gemm_format(const w4a8_weight* w, int act) {
+    return w->group == 128 && !w->has_min && act == W4A8_ACT_TOKEN && w->k % 128 == 0;
+}
 
 // Group-128 weights with per-token activations go to the tensor-core GEMV;
 // everything else (the engine's group-32 format, per-32 activations) to the dp4a one.
@@ -106,6 +114,8 @@ const char* w4a8_version(void) { return "webyiq-b200 w4a8 0.1 (sm_100a)"; }
 void w4a8_set_pdl(int enable) { g_use_pdl = enable ? 1 : 0; }
 
 void w4a8_set_gemv_kernel(int tensor_core) { g_use_mma = tensor_core ? 1 : 0; }
+
+void w4a8_set_gemm_kernel(int tensor_core) { g_use_tc_gemm = tensor_core ? 1 : 0; }
 
 w4a8_status w4a8_device_error(uint32_t* code, void* stream) {
     return device_error(code, static_cast<cudaStream_t>(stream));
@@ -181,6 +191,10 @@ w4a8_status w4a8_gemm(const w4a8_weight* w, const int8_t* xq, const float* xs, i
     if (m < 1) return set_error(W4A8_EINVAL, "w4a8_gemm: m=%d", m);
     if (mode < W4A8_STORE || mode > W4A8_SWIGLU) return set_error(W4A8_EINVAL, "w4a8_gemm: mode=%d", mode);
     if (mode == W4A8_SWIGLU && w->n % 2) return set_error(W4A8_EINVAL, "w4a8_gemm: SWIGLU needs even n (%d)", w->n);
+    if (g_use_tc_gemm && tc_gemm_format(w, act)) {
+        if (!aligned(y, 4)) return set_error(W4A8_EINVAL, "w4a8_gemm: y misaligned");
+        return launch_gemm_tc(w, xq, xs, m, mode, y, nullptr, static_cast<cudaStream_t>(stream));
+    }
     // Token blocks of up to 16 through the GEMV kernels.
     const int n_out = mode == W4A8_SWIGLU ? w->n / 2 : w->n;
     for (int t0 = 0; t0 < m; t0 += W4A8_GEMV_MAX_M) {
@@ -191,6 +205,17 @@ w4a8_status w4a8_gemm(const w4a8_weight* w, const int8_t* xq, const float* xs, i
         if (st != W4A8_OK) return st;
     }
     return W4A8_OK;
+}
+
+w4a8_status w4a8_gemm_group_dots(const w4a8_weight* w, const int8_t* xq, int32_t m, int32_t* dots, void* stream) {
+    w4a8_status st = check_weight(w, "w4a8_gemm_group_dots");
+    if (st != W4A8_OK) return st;
+    if (!xq || !dots || !aligned(xq, 16) || !aligned(dots, 4))
+        return set_error(W4A8_EINVAL, "w4a8_gemm_group_dots: bad xq/dots");
+    if (m < 1) return set_error(W4A8_EINVAL, "w4a8_gemm_group_dots: m=%d", m);
+    if (!tc_gemm_format(w, W4A8_ACT_TOKEN))
+        return set_error(W4A8_ENOTSUP, "w4a8_gemm_group_dots: group-128 symmetric weights only");
+    return launch_gemm_tc(w, xq, nullptr, m, W4A8_STORE, nullptr, dots, static_cast<cudaStream_t>(stream));
 }
 
 w4a8_status w4a8_matmul(const w4a8_weight* w, const int8_t* xq, const float* xs, int32_t act, int32_t m, int32_t mode,

@@ -89,6 +89,20 @@ w4a8_status launch_gemv_mma(const GemvParams& g, bool has_min, int mode, int out
     return W4A8_OK;
 }
 
+// Device address of the error word, for kernels compiled in other files (each
+// file has its own __device__ variables, so they take it as a parameter).
+unsigned int* device_error_word() {
+    static unsigned int* addr[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_w4a8_dev_error) != cudaSuccess) return nullptr;
+        addr[dev] = static_cast<unsigned int*>(p);
+    }
+    return addr[dev];
+}
+
 w4a8_status device_error(unsigned int* code, cudaStream_t st) {
     unsigned int v = 0;
     cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_w4a8_dev_error, sizeof(v), 0, cudaMemcpyDeviceToHost, st);

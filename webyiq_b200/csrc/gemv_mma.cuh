@@ -32,6 +32,7 @@
 #pragma once
 
 #include "gemv.cuh"
+#include "tma.cuh"
 
 namespace w4a8 {
 
@@ -39,12 +40,10 @@ constexpr int kMmaMaxWarps = 16;
 constexpr int kMmaGPS = 4;      // groups per K-slice task
 constexpr int kMmaTokens = 8;   // tokens per launch (the mma N)
 constexpr int kMmaMaxStages = 3;
-constexpr long long kWaitLimitCycles = 1ll << 29;  // bounded waits: ~0.3 s at 2 GHz
 
 // Set (atomicOr) by a kernel whose bounded wait gave up; read and cleared by
 // w4a8_device_error.  Defined here: only gemv_mma.cu includes this header.
 __device__ unsigned int g_w4a8_dev_error = 0;
-enum : unsigned int { DEV_ERR_TMA_TIMEOUT = 1u };
 
 struct MmaParams {
     const uint4* q;        // [rows, k/32] 16-byte chunks
@@ -105,53 +104,6 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, 
     asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
                  : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-// --- TMA bulk copies and mbarriers (no cluster multicast anywhere) -----------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_init_fence() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-// Orders this thread's earlier generic-proxy shared-memory accesses before
-// later async-proxy (TMA) accesses.
-__device__ __forceinline__ void fence_proxy_async() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-__device__ __forceinline__ void tma_bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
-// Wait for phase `parity` of the barrier, giving up after kWaitLimitCycles: a
-// non-blocking test first (the phase is usually complete by now), then the
-// hardware-suspending try_wait, so a waiting thread does not spin on the issue port.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    const uint32_t a = smem_u32(bar);
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-    const long long t0 = clock64();
-    while (true) {
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(done)
-            : "r"(a), "r"(parity)
-            : "memory");
-        if (done) return true;
-        if (clock64() - t0 > kWaitLimitCycles) return false;
-    }
 }
 
 // One token: 64 registers, so the next kernel's CTA fits beside this one and its

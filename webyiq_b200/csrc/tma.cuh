@@ -1,0 +1,64 @@
+// Shared-memory barriers, TMA copies and the device error word's codes, shared by
+// the tensor-core kernels.  No copy here uses cluster multicast.
+#pragma once
+
+#include <cstdint>
+
+namespace w4a8 {
+
+constexpr long long kWaitLimitCycles = 1ll << 29;  // bounded waits: ~0.3 s at 2 GHz
+
+// Bits of the device error word (set by a kernel whose bounded wait gave up).
+enum : unsigned int {
+    DEV_ERR_TMA_TIMEOUT = 1u,   // GEMV: a weight copy never landed
+    DEV_ERR_GEMM_TIMEOUT = 2u,  // GEMM: a pipeline wait gave up
+};
+
+// --- TMA bulk copies and mbarriers (no cluster multicast anywhere) -----------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// Orders this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (TMA) accesses.
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tma_bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+// Wait for phase `parity` of the barrier, giving up after kWaitLimitCycles: a
+// non-blocking test first (the phase is usually complete by now), then the
+// hardware-suspending try_wait, so a waiting thread does not spin on the issue port.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    const long long t0 = clock64();
+    while (true) {
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (clock64() - t0 > kWaitLimitCycles) return false;
+    }
+}
+
+}  // namespace w4a8

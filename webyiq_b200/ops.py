@@ -121,6 +121,15 @@ def group_dots(w, xq):
     return dots
 
 
+def gemm_group_dots(w, xq):
+    """The tcgen05 GEMM's int32 group dots (read back from tensor memory): int32 [m, n, k/128]."""
+    _need_cuda(xq)
+    m = xq.shape[0]
+    dots = torch.empty((m, w.n, w.k // w.group), dtype=torch.int32, device=xq.device)
+    _lib.check(_lib.load().w4a8_gemm_group_dots(ctypes.byref(w.c), _ptr(xq), m, _ptr(dots), _stream()))
+    return dots
+
+
 def lmhead_workspace(w, m, device):
     nbytes = _lib.load().w4a8_lmhead_workspace_bytes(w.n, m)
     return torch.zeros(nbytes, dtype=torch.uint8, device=device)
@@ -180,3 +189,8 @@ def device_error():
 def set_gemv_kernel(tensor_core):
     """Group-128 per-token GEMVs on the tensor-core kernel (True) or dp4a (False)."""
     _lib.load().w4a8_set_gemv_kernel(1 if tensor_core else 0)
+
+
+def set_gemm_kernel(tensor_core):
+    """GEMMs the tcgen05 kernel covers on it (True) or on GEMV token blocks (False)."""
+    _lib.load().w4a8_set_gemm_kernel(1 if tensor_core else 0)
