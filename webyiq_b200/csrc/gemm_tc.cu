@@ -1,43 +1,51 @@
-// W4A8 prefill GEMM on the 5th-generation tensor cores: tcgen05.mma kind::i8 with
-// the accumulators in tensor memory (TMEM), for group-128 symmetric int4 weights
-// and per-token int8 activations:
+// W4A8 prefill GEMM on the 5th-generation tensor cores: tcgen05.mma kind::i8 on
+// SM pairs (cta_group::2) with the accumulators in tensor memory (TMEM), for
+// group-128 symmetric int4 weights and per-token int8 activations:
 //
 //     y[m, n] = dx[m] * sum_g s[n, g] * I[m, n, g],   I = sum_{k in g} (q[n,k] - 8) * xq[m, k]
 //
 // Reference: gemm_q4q8.wgsl:46-121 (the tiled prefill GEMM; its per-group math is
 // the GEMV's, gemv_q4q8.wgsl:29-34,68, and the output modes are those of
 // gemv_q4q8.wgsl:122-129).  The per-group int32 dots I are exact; the scale step
-// is fp32 (y within 1e-6 relative of the exact path), not the bit-exact int64
+// is f32 (y within 1e-6 relative of the exact path), not the bit-exact int64
 // step of the GEMV kernels.
 //
 // Why this shape (B200 view).
-//  - Weight rows are the MMA M (128, one TMEM lane per row) and tokens the MMA N
-//    (128 columns).  The per-group scale s[n, g] is then a per-lane constant, so
-//    the epilogue thread that owns a row multiplies every column it reads by one
-//    register.
-//  - The int4 -> int8 step writes 16*(q-8) into each byte: the nibble q^8 (the
-//    4-bit two's complement of q-8) lands in the high half of the byte, so its
-//    sign extends for free; the factor 16 is folded into the scale (exact).  One
-//    packed word becomes two int8 words in three logic operations.
-//  - The scale step needs the group's int32 dots as floats.  Each TMEM
-//    accumulator is pre-set to the bits of 1.5*2^23 and the MMA adds the group's
-//    dots onto it (|16 I| < 2^22), so the accumulator read back as a float is
-//    exactly 1.5*2^23 + 16 I; one packed subtract and one packed FMA per two
-//    values finish the step, and writing the bias back re-arms the buffer.
-//  - Four TMEM buffers of 128 columns (all 512) hold consecutive groups, so the
-//    tensor core runs up to four groups ahead of the epilogue.  Shared memory
-//    holds four stages of the pipeline: the packed weight tile (TMA), its int8
-//    expansion (written by the dequant warps in the 128-byte-swizzled K-major
-//    layout the MMA descriptor names) and the activation tile (TMA, 128-byte
-//    swizzle).  Each CTA is persistent over tiles; the last tile's output stores
-//    overlap the next tile's first MMAs.
+//  - A cluster of two CTAs (two SMs) computes a tile of 256 weight rows x 128
+//    tokens with one tcgen05.mma.cta_group::2 per 32-deep k-step (M = 256 rows,
+//    N = 128 tokens).  Each SM holds 128 weight rows and HALF of the activation
+//    tile (64 tokens); the pair's tensor cores share both halves.  So an SM
+//    brings in 8 KB of packed weights and 8 KB of activations per 128-deep group
+//    (16 KB, a third less than a one-SM 128 x 128 tile), which is what the L2 ->
+//    SM path can sustain at tensor-core speed.
+//  - Weight rows are the MMA M (one TMEM lane per row), tokens the MMA N: the
+//    per-group scale s[n, g] is a per-lane constant in the epilogue.
+//  - The packed weights go straight from global memory into registers of the
+//    expansion warps (two groups ahead, so their latency is hidden), which write
+//    16*(q-8) per byte into the K-major 128-byte-swizzled A tile: the nibble q^8
+//    (the 4-bit two's complement of q-8) lands in the high half of the byte, so
+//    its sign extends for free; the factor 16 is folded into the scale (exact).
+//    No shared-memory copy of the packed weights is made: shared-memory bandwidth
+//    is the other limit of this kernel.
+//  - Activations come by TMA, four groups (4 x 8 KB) per copy through a 3-D
+//    tensor map (k-inner 128 bytes, tokens, groups), so every group lands as its
+//    own swizzled K-major block.
+//  - Each TMEM accumulator is pre-set to the bits of 1.5*2^23 and the MMA adds the
+//    group's dots onto it (|16 I| < 2^22), so the accumulator read back as a float
+//    is exactly 1.5*2^23 + 16 I; one packed subtract and one packed FMA per two
+//    values finish the scale step, and writing the bias back re-arms the buffer.
+//    Four TMEM buffers of 128 columns (all 512) let the tensor core run four
+//    groups ahead of the epilogue.
 //
-// Warp roles (12 warps, 168 registers each): warp 0 lane 0 is the scheduler, a
-// loop that issues TMA copies and MMAs as soon as their barriers allow (non-
-// blocking tests, so neither waits behind the other); warps 1-3 expand int4 to
-// int8; warps 4-11 are the epilogue (two halves of 64 columns; warp % 4 is the
-// TMEM lane quadrant a warp may read).  Every wait is bounded; a wait that gives
-// up sets the device error word, and all roles then leave their loops.
+// Warp roles per CTA (12 warps, 168 registers each): 0 activation TMA, 1 MMA
+// issue (cluster rank 0 only; a tcgen05.mma blocks its thread for about its own
+// duration) and TMEM allocation, 2-3 int4 -> int8 expansion, 4-11 epilogue (two
+// halves of 64 columns; warp % 4 is the TMEM lane quadrant a warp may read).
+// Barriers that the MMA waits on (int8 tiles written, accumulators released)
+// live in rank 0 and both CTAs arrive on them; the MMA's completions arrive on
+// both CTAs' barriers (one tcgen05.commit per CTA).  Every wait is bounded; a wait
+// that gives up sets the device error word and all roles then leave their loops.
+// Nothing here uses cluster multicast.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
@@ -50,35 +58,38 @@
 
 namespace w4a8 {
 
-int sm_count();                    // capi.cu
+int sm_count();                     // capi.cu
 unsigned int* device_error_word();  // gemv_mma.cu
 
 namespace {
 
-constexpr int kRows = 128;  // weight rows per tile (MMA M)
-constexpr int kTok = 128;   // tokens per tile (MMA N)
-constexpr int kLoadStages = 6;  // packed weight + activation tiles (TMA ring)
-constexpr int kAStages = 3;     // int8 weight tiles (expansion ring)
-constexpr int kBufs = 4;        // TMEM group accumulators of kTok columns
-constexpr uint32_t kTmemCols = kBufs * kTok;
-constexpr int kDeqWarp0 = 1, kDeqWarps = 3;
-constexpr int kDeqThreads = kDeqWarps * 32;
+constexpr int kRows = 128;      // weight rows per CTA (half of the MMA M = 256)
+constexpr int kTok = 128;       // tokens per tile (the MMA N); each CTA loads half
+constexpr int kHalfTok = kTok / 2;
+constexpr int kSG = 4;          // groups per pipeline stage (one weight and one activation copy)
+constexpr int kStages = 3;
+constexpr int kDBufs = 3;       // TMEM group accumulators of kTok columns
+constexpr int kABufs = 4;       // TMEM int8 weight tiles of 32 columns (128 rows x 128 k)
+constexpr int kLead = 2;        // groups the weight expansion runs ahead of the scale step
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemA = kDBufs * kTok;  // first column of the weight tiles
+static_assert(kTmemA + kABufs * 32 <= kTmemCols, "TMEM plan exceeds 512 columns");
+static_assert(kLead < kABufs && kLead < kDBufs + 1, "expansion lead exceeds the buffers");
 constexpr int kEpiWarp0 = 4, kEpiWarps = 8;
 constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 384: 168 registers per thread
-constexpr uint32_t kBias = 0x4B400000u;  // bits of 1.5 * 2^23
+constexpr uint32_t kBias = 0x4B400000u;                  // bits of 1.5 * 2^23
 constexpr float kBiasF = 12582912.0f;
 
-constexpr uint32_t kXBytes = kTok * 128;   // activation tile: kTok rows x 128 k
-constexpr uint32_t kABytes = kRows * 128;  // int8 weight tile: kRows x 128 k
-constexpr uint32_t kPBytes = kRows * 64;   // packed weight tile: kRows x 64 bytes
-constexpr uint32_t kOffX = 0;
-constexpr uint32_t kOffP = kOffX + kLoadStages * kXBytes;
-constexpr uint32_t kOffA = kOffP + kLoadStages * kPBytes;
-constexpr uint32_t kOffXchg = kOffA + kAStages * kABytes;
+constexpr uint32_t kWGroupBytes = kRows * 64;       // packed weights of one group (this CTA's rows)
+constexpr uint32_t kXGroupBytes = kHalfTok * 128;   // activations of one group (this CTA's tokens)
+constexpr uint32_t kStageBytes = kSG * (kWGroupBytes + kXGroupBytes);
+constexpr uint32_t kOffW = 0;                       // [stage][group][128 rows][64 B], 64-byte swizzle
+constexpr uint32_t kOffX = kStages * kSG * kWGroupBytes;  // [stage][group][64 tokens][128 B], 128-byte swizzle
+constexpr uint32_t kOffXchg = kOffX + kStages * kSG * kXGroupBytes;
 constexpr uint32_t kXchgBytes = 2 * 64 * 64 * 4;  // SWIGLU: up-half values of both column halves
 
 __host__ __device__ constexpr uint32_t bar_offset(bool swiglu) { return kOffXchg + (swiglu ? kXchgBytes : 0); }
-__host__ __device__ constexpr size_t smem_bytes(bool swiglu) { return 1024 + bar_offset(swiglu) + 256; }
+__host__ __device__ constexpr size_t smem_bytes(bool swiglu) { return 1024 + bar_offset(swiglu) + 512; }
 static_assert(smem_bytes(true) <= 227 * 1024, "shared memory plan exceeds 227 KB");
 
 struct TcParams {
@@ -93,17 +104,40 @@ struct TcParams {
     int row_tiles, tok_tiles;
 };
 
-// --- tcgen05 / TMA primitives -------------------------------------------------
+// --- cluster / tcgen05 / TMA primitives -----------------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+// Arrival on a barrier of either CTA of the cluster (address from peer_addr).  The
+// data it publishes is in tensor memory, ordered by the tcgen05 fences around the
+// arrival and the wait, so the arrival keeps the default CTA-scope release: a
+// cluster-scope release would also wait for this thread's outstanding global loads.
+__device__ __forceinline__ void arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t cols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols)
+// Pair-wide TMEM allocation: the same warp of both CTAs executes it.
+__device__ __forceinline__ void tmem_alloc2(uint32_t* slot, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols)
                  : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
 }
 
 // K-major operand in the 128-byte swizzle: rows of 128 bytes, 8-row atoms 1024
@@ -117,29 +151,36 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return d;
 }
 
-// kind::i8 instruction descriptor: s32 accumulate, signed A and B, both K-major.
+// kind::i8 instruction descriptor: s32 accumulate, signed A and B, both K-major,
+// M = 256 (the pair), N = kTok.
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kTok >> 3) << 17) |
-                            (static_cast<uint32_t>(kRows >> 4) << 24);
+                            (static_cast<uint32_t>(256 >> 4) << 24);
 
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+// One k-step of the pair's MMA: A (this CTA's 128 weight rows, int8) from TMEM,
+// B (this CTA's 64 tokens) from shared memory.
+__device__ __forceinline__ void mma_i8_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, 1, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc)
+        " tcgen05.mma.cta_group::2.kind::i8 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc)
         : "memory");
 }
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+// Arrives on the barrier at this shared::cluster address (either CTA of the pair)
+// once the MMAs issued so far complete.
+__device__ __forceinline__ void tc_commit_to(uint32_t cluster_addr) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
                  : "memory");
 }
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+// The same barrier in both CTAs: one commit per CTA.
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
+    tc_commit_to(peer_addr(bar, 0));
+    tc_commit_to(peer_addr(bar, 1));
 }
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
             smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
         : "memory");
 }
 
@@ -158,6 +199,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// 16 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
 // Writes the bias into 32 consecutive columns of this thread's lane.
 __device__ __forceinline__ void tmem_bias32(uint32_t taddr) {
     const uint32_t b = kBias;
@@ -168,74 +218,62 @@ __device__ __forceinline__ void tmem_bias32(uint32_t taddr) {
         : "memory");
 }
 
-// Barrier over the 128 threads of one epilogue column half (an mbarrier, so the
-// wait is bounded like every other wait here).
-__device__ __forceinline__ bool half_sync(uint64_t* bar, uint32_t& phase, volatile int* abort_flag,
-                                          unsigned int* err) {
-    mbar_arrive(bar);
-    const bool ok = mbar_wait(bar, phase & 1);
-    ++phase;
-    if (!ok) {
-        *abort_flag = 1;
-        atomicOr(err, DEV_ERR_GEMM_TIMEOUT);
-    }
-    return ok;
-}
-
 // 16 * (q - 8) for the four low nibbles / the four high nibbles of a packed word.
 __device__ __forceinline__ uint32_t expand_lo(uint32_t w) { return ((w ^ 0x88888888u) << 4) & 0xF0F0F0F0u; }
 __device__ __forceinline__ uint32_t expand_hi(uint32_t w) { return (w ^ 0x88888888u) & 0xF0F0F0F0u; }
 
-// A bounded wait that turns a timeout into the error word and the abort flag.
-__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned int* err) {
-    if (mbar_wait(bar, parity)) return true;
-    *abort_flag = 1;
-    atomicOr(err, DEV_ERR_GEMM_TIMEOUT);
-    return false;
-}
-
-__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return done != 0;
-}
+// Bounded waits that turn a timeout into the error word and the abort flag.
+struct Abort {
+    volatile int* flag;
+    unsigned int* err;
+    __device__ bool fail() const {
+        *flag = 1;
+        atomicOr(err, DEV_ERR_GEMM_TIMEOUT);
+        return false;
+    }
+    __device__ bool wait(uint64_t* bar, uint32_t parity) const { return mbar_wait(bar, parity) || fail(); }
+    // Barrier over the 128 threads of one epilogue column half (bounded, unlike a
+    // named barrier).
+    __device__ bool half_sync(uint64_t* bar, uint32_t& phase) const {
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+        const bool ok = mbar_wait(bar, phase & 1);
+        ++phase;
+        return ok || fail();
+    }
+};
 
 template <int MODE, bool DOTS>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                    const TcParams p) {
     constexpr bool SWI = (MODE == W4A8_SWIGLU);
-    constexpr int kOutRows = SWI ? 64 : kRows;  // output rows per tile
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + bar_offset(SWI));  // TMA landed
-    uint64_t* empty = full + kLoadStages;   // MMA done with the load stage
-    uint64_t* aready = empty + kLoadStages; // int8 tile written
-    uint64_t* aempty = aready + kAStages;   // MMA done with the int8 tile
-    uint64_t* accf = aempty + kAStages;     // group accumulator complete
-    uint64_t* acce = accf + kBufs;          // group accumulator read and re-biased
-    uint64_t* done = acce + kBufs;
-    uint64_t* xbar = done + 1;  // SWIGLU exchange, one per column half
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + bar_offset(SWI));  // stage copies landed (local)
+    uint64_t* empty = full + kStages;     // MMA done with a stage (both)
+    uint64_t* aready = empty + kStages;   // int8 weight tile written to TMEM (rank 0; both CTAs arrive)
+    uint64_t* aempty = aready + kABufs;   // MMA done with an int8 weight tile (both)
+    uint64_t* accf = aempty + kABufs;     // group accumulator complete (both)
+    uint64_t* acce = accf + kDBufs;       // accumulator read and re-biased (rank 0; both arrive)
+    uint64_t* done = acce + kDBufs;       // all MMAs complete (rank 0)
+    uint64_t* xbar = done + 1;            // SWIGLU exchange, one per column half (local)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kLoadStages; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(full + s, 1);
             mbar_init(empty + s, 1);
         }
-        for (int s = 0; s < kAStages; ++s) {
-            mbar_init(aready + s, kDeqThreads);
-            mbar_init(aempty + s, 1);
+        for (int a = 0; a < kABufs; ++a) {
+            mbar_init(aready + a, 2 * kEpiWarps);  // one arrival per epilogue warp of each CTA
+            mbar_init(aempty + a, 1);
         }
-        for (int b = 0; b < kBufs; ++b) {
+        for (int b = 0; b < kDBufs; ++b) {
             mbar_init(accf + b, 1);
-            mbar_init(acce + b, kEpiWarps * 32);
+            mbar_init(acce + b, 2 * kEpiWarps);
         }
         mbar_init(done, 1);
         mbar_init(xbar, 128);
@@ -243,235 +281,286 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 0;
         mbar_init_fence();
     }
-    if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
+    if (warp == 1) tmem_alloc2(tmem_slot, kTmemCols);
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     pdl_launch_dependents();
     pdl_wait();
 
+    const Abort ab{abort_flag, p.err};
+    const int nclusters = gridDim.x / 2;
+    const int cluster = blockIdx.x / 2;
     const int tiles = p.row_tiles * p.tok_tiles;
+    const int my_tiles = cluster < tiles ? (tiles - 1 - cluster) / nclusters + 1 : 0;
     const int kg = p.kg;
+    const int spt = (kg + kSG - 1) / kSG;  // stages per tile
+    // First weight row of this CTA's 128 (SWIGLU: first gate row of its 64 outputs).
+    auto row0_of = [&](int t) -> int {
+        const int rt = t / p.tok_tiles;
+        return SWI ? rt * 128 + static_cast<int>(rank) * 64 : rt * 256 + static_cast<int>(rank) * kRows;
+    };
 
     if (warp == 0) {
-        // ---- scheduler: TMA copies up to kLoadStages groups ahead, MMAs in order ----
+        // ---- TMA: kSG groups of this CTA's packed weight rows and its 64 tokens per stage ----
         if (lane == 0) {
-            const int my_tiles = blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-            const uint32_t total = static_cast<uint32_t>(my_tiles) * kg;
-            uint32_t tj = 0, mj = 0;  // next group to copy / to multiply
-            int tg = 0, tt = blockIdx.x;  // group and tile of tj
-            long long idle_since = clock64();
-            while (mj < total) {
-                bool progress = false;
-                while (tj < total) {
-                    const uint32_t s = tj % kLoadStages, u = tj / kLoadStages;
-                    if (!mbar_test(empty + s, (u & 1) ^ 1)) break;
-                    const int n0 = (tt / p.tok_tiles) * kOutRows, m0 = (tt % p.tok_tiles) * kTok;
-                    mbar_expect_tx(full + s, kPBytes + kXBytes);
-                    unsigned char* pk = smem + kOffP + s * kPBytes;
+            uint32_t js = 0;
+            bool ok = true;
+            for (int i = 0; i < my_tiles && ok; ++i) {
+                const int t = cluster + i * nclusters;
+                const int r0 = row0_of(t);
+                const int m0 = (t % p.tok_tiles) * kTok + static_cast<int>(rank) * kHalfTok;
+                for (int st = 0; st < spt; ++st, ++js) {
+                    const uint32_t s = js % kStages, u = js / kStages;
+                    if (*abort_flag || !ab.wait(empty + s, (u & 1) ^ 1)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(full + s, kStageBytes);
+                    unsigned char* w = smem + kOffW + s * kSG * kWGroupBytes;
                     if (SWI) {
-                        tma_load_2d(pk, &tm_w, tg * 64, n0, full + s);
-                        tma_load_2d(pk + 64 * 64, &tm_w, tg * 64, p.n_out + n0, full + s);
+                        tma_load_3d(w, &tm_w, 0, r0, st * kSG, full + s);
+                        tma_load_3d(w + kSG * kWGroupBytes / 2, &tm_w, 0, p.n_out + r0, st * kSG, full + s);
                     } else {
-                        tma_load_2d(pk, &tm_w, tg * 64, n0, full + s);
+                        tma_load_3d(w, &tm_w, 0, r0, st * kSG, full + s);
                     }
-                    tma_load_2d(smem + kOffX + s * kXBytes, &tm_x, tg * 128, m0, full + s);
-                    ++tj;
-                    if (++tg == kg) {
-                        tg = 0;
-                        tt += gridDim.x;
-                    }
-                    progress = true;
+                    tma_load_3d(smem + kOffX + s * kSG * kXGroupBytes, &tm_x, 0, m0, st * kSG, full + s);
                 }
-                if (mj < tj) {
-                    const uint32_t s = mj % kLoadStages, u = mj / kLoadStages;
-                    const uint32_t sa = mj % kAStages, ua = mj / kAStages;
-                    const uint32_t b = mj % kBufs, v = mj / kBufs;
-                    if (mbar_test(aready + sa, ua & 1) && mbar_test(full + s, u & 1) && mbar_test(acce + b, v & 1)) {
-                        tc_fence_after();
-                        const uint32_t a_addr = smem_u32(smem + kOffA + sa * kABytes);
-                        const uint32_t x_addr = smem_u32(smem + kOffX + s * kXBytes);
-                        const uint32_t d = tmem + b * kTok;
+            }
+            // No copy may still be landing in shared memory when the CTA exits.
+            for (uint32_t i = js > kStages ? js - kStages : 0; i < js; ++i)
+                mbar_wait(full + i % kStages, (i / kStages) & 1);
+        }
+    } else if (warp == 1) {
+        // ---- MMA issue (rank 0): four k-steps of 32 per group for the pair ----
+        // (Both CTAs' epilogue threads saw the group's stage land before they
+        // arrived on aready, so aready covers the activation tile halves too.)
+        if (rank == 0 && lane == 0) {
+            uint32_t j = 0, js = 0;
+            bool ok = true;
+            for (int i = 0; i < my_tiles && ok; ++i) {
+                for (int g = 0; g < kg; ++g, ++j) {
+                    const uint32_t s = js % kStages;
+                    const uint32_t a = j % kABufs, ua = j / kABufs;
+                    const uint32_t b = j % kDBufs, v = j / kDBufs;
+                    if (*abort_flag || !ab.wait(aready + a, ua & 1) || !ab.wait(acce + b, v & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t x_addr = smem_u32(smem + kOffX + (s * kSG + g % kSG) * kXGroupBytes);
+                    const uint32_t d = tmem + b * kTok;
+                    const uint32_t at = tmem + kTmemA + a * 32;
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            mma_i8(d, sw128_desc(a_addr + 32 * kk), sw128_desc(x_addr + 32 * kk), kIdesc);
-                        tc_commit(empty + s);
-                        tc_commit(aempty + sa);
-                        tc_commit(accf + b);
-                        ++mj;
-                        progress = true;
+                    for (int kk = 0; kk < 4; ++kk) mma_i8_pair_ts(d, at + kk * 8, sw128_desc(x_addr + 32 * kk), kIdesc);
+                    tc_commit_pair(aempty + a);
+                    tc_commit_pair(accf + b);
+                    if (g % kSG == kSG - 1 || g == kg - 1) {
+                        tc_commit_pair(empty + s);
+                        ++js;
                     }
                 }
-                if (progress) {
-                    idle_since = clock64();
-                } else if (*abort_flag || clock64() - idle_since > kWaitLimitCycles) {
-                    *abort_flag = 1;
-                    atomicOr(p.err, DEV_ERR_GEMM_TIMEOUT);
-                    break;
-                }
             }
-            // Every MMA issued completes, and no copy is still landing in shared
-            // memory, before TMEM is released and the CTA exits.
-            tc_commit(done);
+            // Every MMA issued completes before TMEM is released.
+            tc_commit_to(peer_addr(done, 0));
             mbar_wait(done, 0);
-            for (uint32_t i = tj > kLoadStages ? tj - kLoadStages : 0; i < tj; ++i)
-                mbar_wait(full + i % kLoadStages, (i / kLoadStages) & 1);
         }
-    } else if (warp < kEpiWarp0) {
-        // ---- int4 -> int8 expansion into the swizzled K-major A tile ----
-        const int dt = threadIdx.x - kDeqWarp0 * 32;
-        uint32_t j = 0;
-        bool ok = true;
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-            for (int g = 0; g < kg; ++g, ++j) {
-                const uint32_t s = j % kLoadStages, u = j / kLoadStages;
-                const uint32_t sa = j % kAStages, ua = j / kAStages;
-                const bool w_ok = !*abort_flag && tc_wait(full + s, u & 1, abort_flag, p.err) &&
-                                  tc_wait(aempty + sa, (ua & 1) ^ 1, abort_flag, p.err);
-                if (!__all_sync(kFull, w_ok)) {
-                    ok = false;
-                    break;
-                }
-                const uint4* src = reinterpret_cast<const uint4*>(smem + kOffP + s * kPBytes);
-                unsigned char* dst = smem + kOffA + sa * kABytes;
-                for (int ci = dt; ci < kRows * 4; ci += kDeqThreads) {
-                    // 16-byte chunk ci: row ci/4, k-words 4(ci%4)..+3 -> int8 chunks 2(ci%4), +1
-                    const int r = ci >> 2, c = ci & 3;
-                    const uint4 w = src[ci];
-                    const uint4 o0 = make_uint4(expand_lo(w.x), expand_hi(w.x), expand_lo(w.y), expand_hi(w.y));
-                    const uint4 o1 = make_uint4(expand_lo(w.z), expand_hi(w.z), expand_lo(w.w), expand_hi(w.w));
-                    *reinterpret_cast<uint4*>(dst + r * 128 + (((2 * c) ^ (r & 7)) << 4)) = o0;
-                    *reinterpret_cast<uint4*>(dst + r * 128 + (((2 * c + 1) ^ (r & 7)) << 4)) = o1;
-                }
-                fence_proxy_async();
-                mbar_arrive(aready + sa);
-            }
-        }
-    } else {
-        // ---- epilogue: scale step per group, output per tile ----
+    } else if (warp >= kEpiWarp0) {
+        // ---- epilogue: weight expansion kLead groups ahead, scale step per group,
+        //      output per tile ----
         const int ew = warp - kEpiWarp0;
         const int quad = warp & 3, half = ew >> 2;
         const int lrow = quad * 32 + lane;  // TMEM lane = tile row of this thread
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
-        for (int b = 0; b < kBufs; ++b) {
-            tmem_bias32(lane_base + b * kTok);
-            tmem_bias32(lane_base + b * kTok + 32);
+        const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+        const uint32_t d_base = tmem + lane_off + half * 64;
+        const uint32_t aready_rank0 = peer_addr(aready, 0);
+        const uint32_t acce_rank0 = peer_addr(acce, 0);
+        for (int b = 0; b < kDBufs; ++b) {
+            tmem_bias32(d_base + b * kTok);
+            tmem_bias32(d_base + b * kTok + 32);
         }
         tmem_wait_st();
         tc_fence_before();
-        for (int b = 0; b < kBufs; ++b) mbar_arrive(acce + b);
+        __syncwarp();
+        if (lane == 0)
+            for (int b = 0; b < kDBufs; ++b) arrive_cluster(acce_rank0 + b * 8);
+
+        const uint32_t total = static_cast<uint32_t>(my_tiles) * kg;
+        // The expansion walks the groups in order: group ge of tile ie, in stage sde
+        // (a running stage index), into TMEM weight tile jd % kABufs.
+        uint32_t jd = 0, sde = 0;
+        int ge = 0;
+        // Expands half (k 64*half .. +63) of this thread's weight row for the next
+        // group of the walk.
+        auto expand = [&]() -> bool {
+            const uint32_t s = sde % kStages, a = jd % kABufs, ua = jd / kABufs;
+            const bool w_ok = ab.wait(full + s, (sde / kStages) & 1) && ab.wait(aempty + a, (ua & 1) ^ 1);
+            if (!__all_sync(kFull, w_ok)) return false;
+            // Packed row lrow of the group: 64 bytes, 16-byte chunks swizzled by (row/2)%4.
+            // A stage holds [kSG groups][128 rows][64 B]; for SWIGLU it holds two such
+            // boxes of 64 rows (gate rows, then up rows).
+            const unsigned char* stage_w = smem + kOffW + s * kSG * kWGroupBytes;
+            const unsigned char* wrow =
+                SWI ? stage_w + (lrow >= 64 ? kSG * kWGroupBytes / 2 : 0) + (ge % kSG) * (kWGroupBytes / 2) + (lrow & 63) * 64
+                    : stage_w + (ge % kSG) * kWGroupBytes + lrow * 64;
+            const int sw = (lrow >> 1) & 3;
+            const uint4 c0 = *reinterpret_cast<const uint4*>(wrow + (((2 * half) ^ sw) << 4));
+            const uint4 c1 = *reinterpret_cast<const uint4*>(wrow + (((2 * half + 1) ^ sw) << 4));
+            const uint32_t v[16] = {expand_lo(c0.x), expand_hi(c0.x), expand_lo(c0.y), expand_hi(c0.y),
+                                    expand_lo(c0.z), expand_hi(c0.z), expand_lo(c0.w), expand_hi(c0.w),
+                                    expand_lo(c1.x), expand_hi(c1.x), expand_lo(c1.y), expand_hi(c1.y),
+                                    expand_lo(c1.z), expand_hi(c1.z), expand_lo(c1.w), expand_hi(c1.w)};
+            tmem_st16(tmem + lane_off + kTmemA + a * 32 + half * 16, v);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) arrive_cluster(aready_rank0 + a * 8);
+            ++jd;
+            if (ge % kSG == kSG - 1 || ge == kg - 1) ++sde;
+            if (++ge == kg) ge = 0;
+            return true;
+        };
+        bool ok = true;
+        for (int l = 0; l < kLead && jd < total && ok; ++l) ok = expand();
 
         float* xchg = reinterpret_cast<float*>(smem + kOffXchg) + half * 64 * 64;
         const float2 nbias = make_float2(-kBiasF, -kBiasF);
         uint32_t xph = 0;
         uint32_t j = 0;
-        bool ok = true;
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-            const int n0 = (t / p.tok_tiles) * kOutRows, m0 = (t % p.tok_tiles) * kTok;
-            int row;
+        for (int i = 0; i < my_tiles && ok; ++i) {
+            const int t = cluster + i * nclusters;
+            const int m0 = (t % p.tok_tiles) * kTok;
+            const int mbase = m0 + half * 64;
+            int row, out_row;
             bool row_ok;
             if (SWI) {
-                const int o = n0 + (lrow & 63);
+                const int o = row0_of(t) + (lrow & 63);
                 row_ok = o < p.n_out;
                 row = lrow < 64 ? o : p.n_out + o;
+                out_row = o;
             } else {
-                row = n0 + lrow;
+                row = row0_of(t) + lrow;
                 row_ok = row < p.rows;
+                out_row = row;
             }
             const uint16_t* srow = p.s + static_cast<size_t>(row_ok ? row : 0) * kg;
+            // dx of this half's 64 tokens: lane i holds tokens mbase+i and mbase+32+i.
+            float dx_lo = 0.f, dx_hi = 0.f;
+            if (!DOTS) {
+                if (mbase + lane < p.m) dx_lo = __ldg(p.dx + mbase + lane);
+                if (mbase + 32 + lane < p.m) dx_hi = __ldg(p.dx + mbase + 32 + lane);
+            }
             float2 acc[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.f, 0.f);
-            float sc_next = row_ok ? __half2float(__ushort_as_half(__ldg(srow))) : 0.f;
-            for (int g = 0; g < kg; ++g, ++j) {
-                const float sc = sc_next * 0.0625f;  // the expansion's factor 16
-                if (g + 1 < kg) sc_next = row_ok ? __half2float(__ushort_as_half(__ldg(srow + g + 1))) : 0.f;
-                const uint32_t b = j % kBufs, v = j / kBufs;
-                const bool w_ok = !*abort_flag && tc_wait(accf + b, v & 1, abort_flag, p.err);
-                if (!__all_sync(kFull, w_ok)) {
-                    ok = false;
-                    break;
-                }
+            for (int e = 0; e < 32; ++e) acc[e] = make_float2(0.f, 0.f);
+
+            // One group: expand the weights of group j + kLead, then wait for this
+            // group's accumulator, read it (re-arming the bias) and do the scale step.
+            auto group = [&](int g, float sc_raw) -> bool {
+                if (jd < total && !expand()) return false;
+                const uint32_t b = j % kDBufs, v = j / kDBufs;
+                ++j;
+                const bool w_ok = ab.wait(accf + b, v & 1);
+                if (!__all_sync(kFull, w_ok)) return false;
                 tc_fence_after();
+                const float sc = sc_raw * 0.0625f;  // the expansion's factor 16
                 const float2 sc2 = make_float2(sc, sc);
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {
                     uint32_t r[32];
-                    const uint32_t ta = lane_base + b * kTok + hh * 32;
+                    const uint32_t ta = d_base + b * kTok + hh * 32;
                     tmem_ld32(ta, r);
                     tmem_wait_ld();
                     tmem_bias32(ta);
                     if (DOTS) {
                         if (row_ok) {
 #pragma unroll
-                            for (int i = 0; i < 32; ++i) {
-                                const int m = m0 + half * 64 + hh * 32 + i;
+                            for (int e = 0; e < 32; ++e) {
+                                const int m = mbase + hh * 32 + e;
                                 if (m < p.m)
                                     p.dots[(static_cast<size_t>(m) * p.rows + row) * kg + g] =
-                                        static_cast<int>(r[i] - kBias) >> 4;
+                                        static_cast<int>(r[e] - kBias) >> 4;
                             }
                         }
                     } else {
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const float2 f = __fadd2_rn(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), nbias);
-                            acc[hh * 16 + i] = __ffma2_rn(f, sc2, acc[hh * 16 + i]);
+                        for (int e = 0; e < 16; ++e) {
+                            const float2 f = __fadd2_rn(make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1])), nbias);
+                            acc[hh * 16 + e] = __ffma2_rn(f, sc2, acc[hh * 16 + e]);
                         }
                     }
                 }
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(acce + b);
+                __syncwarp();
+                if (lane == 0) arrive_cluster(acce_rank0 + b * 8);
+                return true;
+            };
+            // Scales run four groups ahead of their use (an L2 round trip is several
+            // groups long), rotating through four registers so the loop stays rolled
+            // (a compact loop body keeps the instruction cache warm).
+            auto scale = [&](int g) -> float {
+                return (row_ok && g < kg) ? __half2float(__ushort_as_half(__ldg(srow + g))) : 0.f;
+            };
+            float s0 = scale(0), s1 = scale(1), s2 = scale(2), s3 = scale(3);
+#pragma unroll 1
+            for (int g = 0; g < kg && ok; ++g) {
+                ok = group(g, s0);
+                s0 = s1;
+                s1 = s2;
+                s2 = s3;
+                s3 = scale(g + 4);
             }
             if (!ok || DOTS) continue;
+
             // Output: y[m, n] = acc * dx[m]; a warp stores 32 consecutive n per token.
-            const int mbase = m0 + half * 64;
             if (SWI) {
                 if (lrow >= 64) {
 #pragma unroll
-                    for (int i = 0; i < 64; ++i) {
-                        const int m = mbase + i;
-                        const float d = m < p.m ? __ldg(p.dx + m) : 0.f;
-                        const float a = (i & 1) ? acc[i >> 1].y : acc[i >> 1].x;
-                        xchg[i * 64 + (lrow - 64)] = a * d;
+                    for (int e = 0; e < 64; ++e) {
+                        const float d = __shfl_sync(kFull, e < 32 ? dx_lo : dx_hi, e & 31);
+                        const float av = (e & 1) ? acc[e >> 1].y : acc[e >> 1].x;
+                        xchg[e * 64 + (lrow - 64)] = av * d;
                     }
                 }
-                if (!half_sync(xbar + half, xph, abort_flag, p.err)) break;
-                if (lrow < 64 && row_ok) {
-                    const int n = n0 + lrow;
+                if (!ab.half_sync(xbar + half, xph)) break;
+                if (lrow < 64) {
 #pragma unroll
-                    for (int i = 0; i < 64; ++i) {
-                        const int m = mbase + i;
-                        if (m < p.m) {
-                            const float a = ((i & 1) ? acc[i >> 1].y : acc[i >> 1].x) * __ldg(p.dx + m);
-                            p.y[static_cast<size_t>(m) * p.y_stride + n] = silu_mul(a, xchg[i * 64 + lrow]);
+                    for (int e = 0; e < 64; ++e) {
+                        const float d = __shfl_sync(kFull, e < 32 ? dx_lo : dx_hi, e & 31);
+                        const int m = mbase + e;
+                        if (row_ok && m < p.m) {
+                            const float av = ((e & 1) ? acc[e >> 1].y : acc[e >> 1].x) * d;
+                            p.y[static_cast<size_t>(m) * p.y_stride + out_row] = silu_mul(av, xchg[e * 64 + lrow]);
                         }
                     }
                 }
-                if (!half_sync(xbar + half, xph, abort_flag, p.err)) break;
-            } else if (row_ok) {
+                if (!ab.half_sync(xbar + half, xph)) break;
+            } else {
+                const int mlim = p.m - mbase;  // tokens of this half that exist
+                float* dst = p.y + static_cast<size_t>(mbase) * p.y_stride + out_row;
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    const int m = mbase + i;
-                    if (m < p.m) {
-                        const float a = ((i & 1) ? acc[i >> 1].y : acc[i >> 1].x) * __ldg(p.dx + m);
-                        float* dst = p.y + static_cast<size_t>(m) * p.y_stride + row;
+                for (int e = 0; e < 64; ++e) {
+                    const float d = __shfl_sync(kFull, e < 32 ? dx_lo : dx_hi, e & 31);
+                    if (row_ok && e < mlim) {
+                        const float av = ((e & 1) ? acc[e >> 1].y : acc[e >> 1].x) * d;
                         if (MODE == W4A8_ADD)
-                            *dst += a;
+                            *dst += av;
                         else
-                            *dst = a;
+                            *dst = av;
                     }
+                    dst += p.y_stride;
                 }
             }
         }
     }
 
     tc_fence_before();
-    __syncthreads();
-    if (warp == 0) {
+    cluster_sync();  // no CTA leaves while its peer may still signal it
+    if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        tmem_dealloc2(tmem, kTmemCols);
     }
 }
 
@@ -490,17 +579,19 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// Row-major byte matrix [outer][inner] with the given row stride, copied in boxes
-// of box_inner x box_outer bytes.
-w4a8_status encode_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t stride,
-                      uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+// 3-D view (inner bytes of one group, rows, groups) of a row-major byte matrix
+// with `group_bytes` bytes per group and `row_stride` bytes per row, copied in
+// boxes of group_bytes x box_rows x kSG groups: each group lands as its own block.
+w4a8_status encode_grouped(CUtensorMap* map, const void* base, int rows, int groups, int group_bytes, int row_stride,
+                           int box_rows, CUtensorMapSwizzle swizzle) {
     const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
     if (!enc) return set_error(W4A8_ECUDA, "w4a8_gemm: cuTensorMapEncodeTiled unavailable");
-    const cuuint64_t dims[2] = {inner, outer};
-    const cuuint64_t strides[1] = {stride};
-    const cuuint32_t box[2] = {box_inner, box_outer};
-    const cuuint32_t elem[2] = {1, 1};
-    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem,
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(group_bytes), static_cast<cuuint64_t>(rows),
+                                static_cast<cuuint64_t>(groups)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride), static_cast<cuuint64_t>(group_bytes)};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(group_bytes), static_cast<cuuint32_t>(box_rows), kSG};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, elem,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(W4A8_ECUDA, "w4a8_gemm: tensor map encode failed (%d)", static_cast<int>(r));
@@ -510,6 +601,7 @@ w4a8_status encode_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64
 template <int MODE, bool DOTS>
 w4a8_status launch_inst(const CUtensorMap& tw, const CUtensorMap& tx, const TcParams& p, cudaStream_t st) {
     static size_t configured = 0;  // dynamic shared memory set for this instantiation
+    static int max_clusters = 0;   // clusters of this kernel that fit on the GPU at once
     auto kernel = gemm_tc_kernel<MODE, DOTS>;
     const size_t smem = smem_bytes(MODE == W4A8_SWIGLU);
     if (smem > configured) {
@@ -517,10 +609,35 @@ w4a8_status launch_inst(const CUtensorMap& tw, const CUtensorMap& tx, const TcPa
         if (e != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8_gemm: smem attribute: %s", cudaGetErrorString(e));
         configured = smem;
     }
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = g_use_pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    if (max_clusters == 0) {
+        cfg.gridDim = dim3(2 * (sm_count() / 2));
+        int n = 0;
+        const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+        if (e != cudaSuccess || n < 1) {
+            cudaGetLastError();
+            n = sm_count() / 2;
+        }
+        max_clusters = n;
+    }
     const int tiles = p.row_tiles * p.tok_tiles;
-    const int sms = sm_count();
-    const int grid = tiles < sms ? tiles : sms;
-    return launch_pdl("w4a8_gemm (tcgen05)", kernel, dim3(grid), dim3(kThreads), smem, st, tw, tx, p);
+    const int clusters = tiles < max_clusters ? tiles : max_clusters;
+    cfg.gridDim = dim3(2 * clusters);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tw, tx, p);
+    if (e != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8_gemm (tcgen05): launch failed: %s", cudaGetErrorString(e));
+    return W4A8_OK;
 }
 
 }  // namespace
@@ -542,14 +659,16 @@ w4a8_status launch_gemm_tc(const w4a8_weight* w, const int8_t* xq, const float* 
     p.m = m;
     p.kg = w->k / 128;
     p.y_stride = p.n_out;
-    p.row_tiles = (p.n_out + (swi ? 63 : 127)) / (swi ? 64 : 128);
+    p.row_tiles = swi ? (p.n_out + 127) / 128 : (p.n_out + 255) / 256;
     p.tok_tiles = (m + kTok - 1) / kTok;
+    // Packed weights: 64 bytes per group and row, boxes of this CTA's 128 rows (64
+    // gate + 64 up rows for SWIGLU), 64-byte swizzle so that one row's chunks are
+    // read without bank conflicts.  Activations: 128 bytes per group and token,
+    // boxes of 64 tokens, 128-byte swizzle (the MMA's K-major layout).
     CUtensorMap tw, tx;
-    w4a8_status s = encode_2d(&tw, w->q, static_cast<uint64_t>(w->k / 2), static_cast<uint64_t>(w->n),
-                              static_cast<uint64_t>(w->k / 2), 64, swi ? 64 : 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+    w4a8_status s = encode_grouped(&tw, w->q, w->n, p.kg, 64, w->k / 2, swi ? 64 : kRows, CU_TENSOR_MAP_SWIZZLE_64B);
     if (s != W4A8_OK) return s;
-    s = encode_2d(&tx, xq, static_cast<uint64_t>(w->k), static_cast<uint64_t>(m), static_cast<uint64_t>(w->k), 128,
-                  kTok, CU_TENSOR_MAP_SWIZZLE_128B);
+    s = encode_grouped(&tx, xq, m, p.kg, 128, w->k, kHalfTok, CU_TENSOR_MAP_SWIZZLE_128B);
     if (s != W4A8_OK) return s;
     if (dots) return launch_inst<W4A8_STORE, true>(tw, tx, p, st);
     if (mode == W4A8_ADD) return launch_inst<W4A8_ADD, false>(tw, tx, p, st);
