@@ -202,6 +202,30 @@ class Sweep:
     launches_per_step = LAYERS * len(SWEEP)
 
 
+def measure_int8_peak(torch, dev, size=8192, reps=5):
+    """Dense int8 tensor-core throughput of the library GEMM (cuBLAS via
+    torch._int_mm) on this GPU, TOPS; None if unavailable."""
+    try:
+        a = torch.randint(-128, 127, (size, size), dtype=torch.int8, device=dev)
+        b = torch.randint(-128, 127, (size, size), dtype=torch.int8, device=dev).t()
+        for _ in range(2):
+            torch._int_mm(a, b)
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        del a, b
+        return 2 * size ** 3 / (best * 1e-3) / 1e12
+    except Exception:
+        return None
+
+
 # ---------------------------------------------------------------------------
 def run_extras(torch, ops, dev, steps, warmup, world, rank, dist):
     """Secondary BASELINE configs, timed with CUDA graphs on this GPU."""
@@ -253,14 +277,20 @@ def run_extras(torch, ops, dev, steps, warmup, world, rank, dist):
     key = torch.empty(1, dtype=torch.int64, device=dev)
     tok = torch.empty(1, dtype=torch.int32, device=dev)
 
+    comm = None
+    if world > 1:
+        # the library's own NCCL communicator (w4a8_lmhead_argmax_allreduce)
+        store = dist.distributed_c10d._get_default_store()
+        if rank == 0:
+            store.set("w4a8_nccl_uid", ops.nccl_unique_id())
+        comm = ops.NcclComm(world, store.get("w4a8_nccl_uid"), rank)
+
     def c3():
-        ops.lmhead_argmax(w, xq, xs, act=ops.ACT_TOKEN, row_offset=rank * per_rank, workspace=wsp,
-                          best_key=key, tok=tok)
-        if world > 1:
-            # keys compare as u64; flip the top bit so the signed max agrees
-            kk = key ^ (-(2 ** 63))
-            dist.all_reduce(kk, op=dist.ReduceOp.MAX)
-            key.copy_(kk ^ (-(2 ** 63)))
+        if comm is None:
+            ops.lmhead_argmax(w, xq, xs, act=ops.ACT_TOKEN, row_offset=0, workspace=wsp, best_key=key, tok=tok)
+        else:
+            ops.lmhead_argmax_allreduce(w, xq, xs, comm, act=ops.ACT_TOKEN, row_offset=rank * per_rank,
+                                        workspace=wsp, best_key=key, tok=tok)
 
     if world > 1:
         # NCCL collectives stay eager (no graph capture across ranks here)
@@ -285,9 +315,14 @@ def run_extras(torch, ops, dev, steps, warmup, world, rank, dist):
     out["c3_lmhead_argmax"] = {"gpus": world, "us_per_token": round(ms * 1e3, 2), "tok_s": round(1e3 / ms, 1),
                                "gbs_total": round(lm_bytes / (ms * 1e-3) / 1e9, 1),
                                "frac_hbm_per_gpu": round(lm_bytes / world / (ms * 1e-3) / 1e9 / hbm, 3),
-                               "collective": "nccl all_reduce(max) of packed u64 keys" if world > 1 else None}
+                               "collective": "w4a8_lmhead_argmax_allreduce: NCCL all-reduce (max, u64) of the "
+                                             "packed keys" if world > 1 else None}
+    if comm is not None:
+        comm.close()
     del w
-    # config 4: prefill GEMM, M = 1024 (rotating over 4 weight copies)
+    # config 4: prefill GEMM, M = 1024 (rotating over 4 weight copies), against the
+    # int8 tensor-core peak measured here with cuBLAS (torch._int_mm)
+    int8_peak = measure_int8_peak(torch, dev)
     c4 = {}
     for k, n in ((2048, 6144), (6144, 2048)):
         ws = [rand_weight(n, k, GROUP, gen, dev, torch, ops) for _ in range(4)]
@@ -301,8 +336,13 @@ def run_extras(torch, ops, dev, steps, warmup, world, rank, dist):
         ms, g = time_graph(torch, c4f, max(steps // 4, 3), min(warmup, 3))
         del g
         per = ms / len(ws)
-        c4[f"{k}x{n}"] = {"us": round(per * 1e3, 2), "tops": round(2 * 1024 * k * n / (per * 1e-3) / 1e12, 1)}
+        tops = 2 * 1024 * k * n / (per * 1e-3) / 1e12
+        c4[f"{k}x{n}"] = {"us": round(per * 1e3, 2), "tops": round(tops, 1),
+                          "frac_int8_peak": round(tops / int8_peak, 3) if int8_peak else None}
         del ws
+    c4["kernel"] = "gemm_tc_kernel: tcgen05.mma.cta_group::2.kind::i8, TMEM accumulators"
+    c4["int8_peak_tops"] = round(int8_peak, 1) if int8_peak else None
+    c4["int8_peak_kind"] = "measured here: cuBLAS int8 GEMM (torch._int_mm) 8192^3, best of 5"
     out["c4_prefill_gemm"] = c4
     return out
 
@@ -515,11 +555,14 @@ def main():
     if rank == 0 and world == 1:
         cpu = cpu_baseline_sample(args.cpu_seconds)
 
+    # DRAM bytes per launch of the sweep's GEMV, from the committed ncu capture of
+    # the same workload (bytes per step / launches per step).
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
         try:
-            traffic = json.load(open(tpath)).get("gemv_decode_sweep_bytes_per_step")
+            per_step = json.load(open(tpath)).get("gemv_decode_sweep_bytes_per_step")
+            traffic = round(per_step / Sweep.launches_per_step) if per_step else None
         except Exception:
             traffic = None
 
@@ -534,7 +577,10 @@ def main():
                        "l2": "inputs larger than L2 (586 MB per step vs 126 MB)",
                        "parallelism": f"replicas x{world}", "launch": "cuda graph, PDL between GEMVs"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(achieved / hbm, 4), "peak_kind": peak_kind, "traffic": traffic},
+                         "frac": round(achieved / hbm, 4), "peak_kind": peak_kind, "traffic": traffic,
+                         "kernel": "gemv_mma_kernel (group-128 per-token GEMV)",
+                         "algorithmic_bytes_per_launch": round(sb / Sweep.launches_per_step),
+                         "launch_us": round(ms * 1e3 / Sweep.launches_per_step, 3)},
             "e2e": {"value": round(e2e, 1), "unit": "GB/s", "ms_per_step": round(ms_e2e, 4),
                     "h2d_bytes_per_step": sweep.nin * 4, "d2h_bytes_per_step": sweep.nout * 4, "mode": e2e_mode},
             "gpu_launches": args.steps * Sweep.launches_per_step,

@@ -166,6 +166,30 @@ W4A8_API w4a8_status w4a8_lmhead_argmax_noalloc(const w4a8_weight* w, int32_t ro
                                                int32_t m, float* logits, uint64_t* best_key,
                                                uint32_t* tok_out, const uint32_t* ids, void* stream);
 
+/* Column-split lm_head over GPUs (head_ops, graph.rs:476-486, with the vocabulary
+ * sharded): this rank's weight holds vocabulary rows [row_offset, row_offset + n);
+ * the call runs w4a8_lmhead_argmax on the shard and then an in-place NCCL
+ * all-reduce (max, u64) of best_key[m] over nccl_comm (an ncclComm_t of all the
+ * ranks that hold shards), so every rank gets the key and token of the global
+ * argmax, bit-identical to one GPU.  tok_out may be NULL; ids (u32[vocab], indexed
+ * by the global row id) or NULL.  Every rank must make the same call with the same
+ * m, on streams the NCCL communicator may use.  W4A8_ENCCL if NCCL cannot be
+ * loaded (libnccl.so.2 is opened at run time) or fails. */
+W4A8_API w4a8_status w4a8_lmhead_argmax_allreduce(const w4a8_weight* w, int32_t row_offset,
+                                                 const int8_t* xq, const float* xs, int32_t act,
+                                                 int32_t m, float* logits, uint64_t* best_key,
+                                                 uint32_t* tok_out, const uint32_t* ids,
+                                                 void* workspace, size_t workspace_bytes,
+                                                 void* nccl_comm, void* stream);
+
+/* NCCL communicator helpers for hosts that do not create one themselves: a
+ * 128-byte unique id made on one rank and given to all, then one communicator per
+ * rank (the calling thread's current CUDA device).  Thin wrappers over
+ * ncclGetUniqueId / ncclCommInitRank / ncclCommDestroy. */
+W4A8_API w4a8_status w4a8_nccl_get_unique_id(void* id_out);
+W4A8_API w4a8_status w4a8_nccl_comm_init(int32_t nranks, const void* id, int32_t rank, void** comm_out);
+W4A8_API w4a8_status w4a8_nccl_comm_destroy(void* comm);
+
 /* Index carried by a packed argmax key (0 for the "no value > -3e38" key 0). */
 static inline uint32_t w4a8_key_index(uint64_t key) {
     return key ? ~(uint32_t)(key & 0xffffffffu) : 0u;

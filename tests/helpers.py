@@ -36,3 +36,29 @@ def assert_rel_close(y, ref, rtol=1e-3):
     assert err.max() <= rtol * scale, f"normwise rel err {err.max() / scale:.3g} > {rtol}"
     bad = err > rtol * np.abs(ref) + rtol * rms
     assert not bad.any(), f"{bad.sum()} elements out of tolerance, worst {err[bad].max():.3g}"
+
+
+def pack_key(v, idx):
+    """Packed argmax key of value v at global index idx, as u64 (argmax.wgsl:17-39
+    order: larger value first, then lower index; NaN and values <= -3e38 give 0)."""
+    v = np.float32(v)
+    if not (v > np.float32(-3e38)):
+        return 0
+    if v == 0:
+        v = np.float32(0.0)
+    b = int(np.array([v], np.float32).view(np.uint32)[0])
+    b = (~b & 0xFFFFFFFF) if b & 0x80000000 else (b | 0x80000000)
+    return (b << 32) | (~int(idx) & 0xFFFFFFFF)
+
+
+def shard_key(logits_row, offset):
+    """Best packed key of one row of a vocabulary shard whose first row is `offset`."""
+    best = 0
+    for j, v in enumerate(logits_row):
+        best = max(best, pack_key(v, offset + j))
+    return best
+
+
+def to_i64(u):
+    """u64 bits as a signed int64 value (for torch int64 tensors)."""
+    return u - (1 << 64) if u >= (1 << 63) else u

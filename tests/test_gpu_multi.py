@@ -1,0 +1,86 @@
+"""The column-split lm_head on 2 GPUs (one rank per GPU): each rank holds half of
+the vocabulary rows and the keys are exchanged (a) through torch.distributed NCCL
+(ops.lmhead_argmax_sharded) and (b) inside the library (w4a8_lmhead_argmax_allreduce
+over its own NCCL communicator).  Both must give the one-device argmax of the
+oracle bit for bit, on every rank.  Skipped with fewer than 2 GPUs."""
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import c as orc
+
+from helpers import make_weight, make_x, shard_key, to_i64
+
+pytestmark = pytest.mark.gpu
+
+V, K, M = 8192, 2048, 3
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _data():
+    q, s, _ = make_weight(V, K, 128, False, seed=11)
+    xq, xs = orc.quant(make_x(M, K, seed=12), act=1)
+    return q, s, xq, xs
+
+
+def _rank(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    from webyiq_b200 import ops
+
+    q, s, xq, xs = _data()
+    per = V // world
+    lo = rank * per
+    qt = torch.from_numpy(np.ascontiguousarray(q[lo:lo + per]).view(np.int32)).to(dev)
+    st = torch.from_numpy(np.ascontiguousarray(s[lo:lo + per]).view(np.int16)).to(dev)
+    w = ops.QWeight(qt, st, per, K, 128, False)
+    xq_d, xs_d = torch.from_numpy(xq).to(dev), torch.from_numpy(xs).to(dev)
+    key1, tok1 = ops.lmhead_argmax_sharded(w, xq_d, xs_d, lo, act=ops.ACT_TOKEN)
+    store = dist.distributed_c10d._get_default_store()
+    if rank == 0:
+        store.set("w4a8_nccl_uid", ops.nccl_unique_id())
+    uid = store.get("w4a8_nccl_uid")
+    comm = ops.NcclComm(world, uid, rank)
+    key2, tok2 = ops.lmhead_argmax_allreduce(w, xq_d, xs_d, comm, act=ops.ACT_TOKEN, row_offset=lo)
+    torch.cuda.synchronize()
+    comm.close()
+    results[rank] = (key1.tolist(), tok1.tolist(), key2.tolist(), tok2.tolist())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_lmhead_split_two_gpus(cuda):
+    world = 2
+    port = _free_port()
+    with mp.get_context("spawn").Manager() as mgr:
+        results = mgr.dict()
+        mp.spawn(_rank, args=(world, port, results), nprocs=world, join=True)
+        got = dict(results)
+    q, s, xq, xs = _data()
+    logits = orc.gemv(q, s, K, 128, False, xq, xs, act=1)
+    ref_tok = orc.argmax(logits).astype(np.int64).tolist()
+    ref_key = [to_i64(shard_key(row, 0)) for row in logits]
+    for r in range(world):
+        key1, tok1, key2, tok2 = got[r]
+        assert key1 == ref_key and key2 == ref_key, r
+        assert tok1 == ref_tok and tok2 == ref_tok, r

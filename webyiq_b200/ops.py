@@ -168,6 +168,83 @@ def lmhead_argmax_noalloc(w, xq, xs, act=ACT_TOKEN, row_offset=0, logits=None, i
     return best_key, tok
 
 
+# ---------------------------------------------------------------------------
+# Column-split lm_head over GPUs (vocabulary rows sharded; one exchange of keys).
+
+_SIGN = -(2 ** 63)
+
+
+def merge_shard_keys(keys, group=None):
+    """All-reduce (max) of packed argmax keys (int64 tensor holding u64 bits) over a
+    torch.distributed group, in place.  Keys compare as unsigned integers; flipping
+    the top bit makes the signed max agree, so any backend (NCCL, gloo) works."""
+    import torch.distributed as dist
+
+    keys ^= _SIGN
+    dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=group)
+    keys ^= _SIGN
+    return keys
+
+
+def keys_to_tokens(keys, ids=None):
+    """Token of every packed key (int64 u64 bits) on the keys' device: the index
+    (~low word, 0 for the key 0), mapped through ids (int32 [vocab]) if given."""
+    low = keys & 0xFFFFFFFF
+    idx = torch.where(keys != 0, 0xFFFFFFFF - low, torch.zeros_like(low))
+    if ids is not None:
+        return ids.to(torch.int64)[idx].to(torch.int32)
+    return idx.to(torch.int32)
+
+
+def lmhead_argmax_sharded(w, xq, xs, row_offset, act=ACT_TOKEN, group=None, ids=None, workspace=None, logits=None):
+    """This rank's vocabulary shard (global rows row_offset .. + w.n) through the
+    fused lm_head argmax, then the keys merged over the torch.distributed group.
+    Returns (best_key int64 [m], tok int32 [m]) of the global argmax on every rank."""
+    best_key, _ = lmhead_argmax(w, xq, xs, act=act, row_offset=row_offset, logits=logits, workspace=workspace)
+    merge_shard_keys(best_key, group)
+    return best_key, keys_to_tokens(best_key, ids)
+
+
+def nccl_unique_id():
+    """128-byte NCCL unique id (make it on one rank, give it to all)."""
+    buf = ctypes.create_string_buffer(128)
+    _lib.check(_lib.load().w4a8_nccl_get_unique_id(buf))
+    return buf.raw
+
+
+class NcclComm:
+    """An NCCL communicator made by the library (for w4a8_lmhead_argmax_allreduce)."""
+
+    def __init__(self, nranks, uid, rank):
+        self.ptr = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(bytes(uid), 128)
+        _lib.check(_lib.load().w4a8_nccl_comm_init(int(nranks), buf, int(rank), ctypes.byref(self.ptr)))
+
+    def close(self):
+        if self.ptr:
+            _lib.check(_lib.load().w4a8_nccl_comm_destroy(self.ptr))
+            self.ptr = ctypes.c_void_p()
+
+
+def lmhead_argmax_allreduce(w, xq, xs, comm, act=ACT_TOKEN, row_offset=0, logits=None, ids=None, workspace=None,
+                            best_key=None, tok=None):
+    """Sharded lm_head with the key exchange inside the library (NCCL all-reduce of
+    the u64 keys over `comm`).  Returns (best_key int64 [m], tok int32 [m])."""
+    _need_cuda(xq, xs, logits, ids, workspace)
+    m = xq.shape[0]
+    dev = xq.device
+    if workspace is None:
+        workspace = lmhead_workspace(w, m, dev)
+    if best_key is None:
+        best_key = torch.empty(m, dtype=torch.int64, device=dev)
+    if tok is None:
+        tok = torch.empty(m, dtype=torch.int32, device=dev)
+    _lib.check(_lib.load().w4a8_lmhead_argmax_allreduce(ctypes.byref(w.c), int(row_offset), _ptr(xq), _ptr(xs), act, m,
+                                                        _ptr(logits), _ptr(best_key), _ptr(tok), _ptr(ids),
+                                                        _ptr(workspace), workspace.numel(), comm.ptr, _stream()))
+    return best_key, tok
+
+
 def key_index(key):
     """Index carried by a packed argmax key (python int, u64 bits)."""
     key &= (1 << 64) - 1
