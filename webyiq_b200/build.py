@@ -81,5 +81,40 @@ def build(verbose=False, jobs=None):
     return LIB
 
 
+HOST = os.path.join(HERE, "host")
+CLI = os.path.join(LIBDIR, "webyiq_cli")
+CXX = os.environ.get("CXX", "g++")
+CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+
+
+def build_host():
+    """Compile the C++ host (host/*.cpp: manifest, engine, Builder, CLI) against the
+    shared library and the CUDA runtime; returns the path of lib/webyiq_cli."""
+    lib = build()
+    srcs = sorted(os.path.join(HOST, f) for f in os.listdir(HOST) if f.endswith(".cpp"))
+    h = hashlib.sha256()
+    for p in srcs + sorted(os.path.join(HOST, f) for f in os.listdir(HOST) if f.endswith(".h")) + \
+            [os.path.join(ROOT, "include", "w4a8.h")]:
+        with open(p, "rb") as f:
+            h.update(p.encode() + f.read())
+    h.update(open(lib + ".stamp").read().encode() if os.path.exists(lib + ".stamp") else b"")
+    key = h.hexdigest()[:16]
+    stamp = CLI + ".stamp"
+    if os.path.exists(CLI) and os.path.exists(stamp) and open(stamp).read() == key:
+        return CLI
+    cmd = [CXX, "-O2", "-std=c++17", "-Wall", "-Wextra", f"-I{os.path.join(ROOT, 'include')}", f"-I{HOST}",
+           f"-I{CUDA_HOME}/include", *srcs, "-o", CLI + ".tmp", f"-L{LIBDIR}", "-lwebyiq_w4a8",
+           f"-L{CUDA_HOME}/lib64", "-lcudart", f"-Wl,-rpath,$ORIGIN:{CUDA_HOME}/lib64"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"host build failed:\n{r.stdout}\n{r.stderr}")
+    os.replace(CLI + ".tmp", CLI)
+    with open(stamp, "w") as f:
+        f.write(key)
+    return CLI
+
+
 if __name__ == "__main__":
     print(build(verbose="-v" in sys.argv))
+    if "--host" in sys.argv:
+        print(build_host())

@@ -87,13 +87,17 @@ class Manifest:
         return raw.view(dt)
 
     def q4(self, name):
-        """(q u32 [n, k/8], s u32 [n, k/group], n, k, group) of a quantized weight `name`."""
+        """(q u32 [n, k/8], s, n, k, group) of a quantized weight `name`; s is u32
+        [n, k/group] (f16 scale | f16 min << 16, convert.py) or, for symmetric
+        weights, u16 [n, k/group] (f16 scale bits)."""
         tq, ts = self.tensors[name + ".q"], self.tensors[name + ".s"]
         n, k = tq["shape"]
-        if k % self.group or tq["bytes"] != n * k // 2 or ts["bytes"] != n * (k // self.group) * 4:
+        kg = k // self.group if self.group else 0
+        if k % self.group or tq["bytes"] != n * k // 2 or ts["bytes"] not in (n * kg * 4, n * kg * 2):
             raise ValueError(f"tensor {name}: sizes do not match shape {n}x{k} group {self.group}")
-        return (self.read(name + ".q").reshape(n, k // 8), self.read(name + ".s").reshape(n, k // self.group),
-                n, k, self.group)
+        s = self.read(name + ".s")
+        s = s.view(np.uint32 if ts["bytes"] == n * kg * 4 else np.uint16).reshape(n, kg)
+        return self.read(name + ".q").reshape(n, k // 8), s, n, k, self.group
 
 
 def write_model(out_dir, tensors, config=None, arch="llama", group=32, scheme="asym-rtn"):
