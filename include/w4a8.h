@@ -229,6 +229,12 @@ W4A8_API void w4a8_set_gemm_kernel(int tensor_core);
  * code may be NULL. */
 W4A8_API w4a8_status w4a8_device_error(uint32_t* code, void* stream);
 
+/* Test hook for the failure path above, without a GPU fault: launches one kernel
+ * whose bounded wait can never complete (nothing arrives on its barrier); it gives
+ * up after ~10 ms and records code 4, so the next w4a8_device_error returns
+ * W4A8_ETIMEOUT with that code and the context stays usable. */
+W4A8_API w4a8_status w4a8_selftest_wait_timeout(void* stream);
+
 /* Message for the last failed call on this thread ("" if none). */
 W4A8_API const char* w4a8_last_error(void);
 

@@ -53,6 +53,7 @@ _SIGS = {
     "w4a8_set_gemm_kernel": (None, [ctypes.c_int]),
     "w4a8_gemm_group_dots": (ctypes.c_int, [ctypes.POINTER(Weight), _P, _I, _P, _P]),
     "w4a8_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), _P]),
+    "w4a8_selftest_wait_timeout": (ctypes.c_int, [_P]),
     "w4a8_last_error": (ctypes.c_char_p, []),
     "w4a8_version": (ctypes.c_char_p, []),
 }

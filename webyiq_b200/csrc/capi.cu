@@ -58,6 +58,7 @@ w4a8_status launch_argmax(const float*, int, int, const uint32_t*, uint32_t*, cu
 
 w4a8_status launch_gemv_mma(const GemvParams& g, bool has_min, int mode, int out, cudaStream_t st);
 w4a8_status device_error(unsigned int* code, cudaStream_t st);
+w4a8_status selftest_wait_timeout(cudaStream_t st);
 w4a8_status launch_gemm_tc(const w4a8_weight* w, const int8_t* xq, const float* dx, int m, int mode, float* y,
                            int* dots, cudaStream_t st);
 
@@ -119,6 +120,10 @@ void w4a8_set_gemm_kernel(int tensor_core) { g_use_tc_gemm = tensor_core ? 1 : 0
 
 w4a8_status w4a8_device_error(uint32_t* code, void* stream) {
     return device_error(code, static_cast<cudaStream_t>(stream));
+}
+
+w4a8_status w4a8_selftest_wait_timeout(void* stream) {
+    return selftest_wait_timeout(static_cast<cudaStream_t>(stream));
 }
 
 w4a8_status w4a8_weight_view(const void* q, const void* s, int32_t n, int32_t k, int32_t group, int32_t has_min,

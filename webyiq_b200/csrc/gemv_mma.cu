@@ -89,6 +89,43 @@ w4a8_status launch_gemv_mma(const GemvParams& g, bool has_min, int mode, int out
     return W4A8_OK;
 }
 
+namespace {
+
+// Failure detection without a fault: one thread waits on an mbarrier that nothing
+// ever arrives on, gives up after `limit` cycles like every wait of the library,
+// records DEV_ERR_SELFTEST and returns; the context stays usable.
+__global__ void selftest_wait_kernel(long long limit) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    const uint32_t a = smem_u32(&bar);
+    const long long t0 = clock64();
+    while (true) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a)
+            : "memory");
+        if (done) return;  // cannot happen: nothing arrives
+        if (clock64() - t0 > limit) {
+            atomicOr(&g_w4a8_dev_error, DEV_ERR_SELFTEST);
+            return;
+        }
+    }
+}
+
+}  // namespace
+
+w4a8_status selftest_wait_timeout(cudaStream_t st) {
+    selftest_wait_kernel<<<1, 32, 0, st>>>(1ll << 24);  // ~10 ms
+    return check_launch("w4a8_selftest_wait_timeout");
+}
+
 // Device address of the error word, for kernels compiled in other files (each
 // file has its own __device__ variables, so they take it as a parameter).
 unsigned int* device_error_word() {

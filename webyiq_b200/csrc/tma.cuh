@@ -12,6 +12,7 @@ constexpr long long kWaitLimitCycles = 1ll << 29;  // bounded waits: ~0.3 s at 2
 enum : unsigned int {
     DEV_ERR_TMA_TIMEOUT = 1u,   // GEMV: a weight copy never landed
     DEV_ERR_GEMM_TIMEOUT = 2u,  // GEMM: a pipeline wait gave up
+    DEV_ERR_SELFTEST = 4u,      // w4a8_selftest_wait_timeout: its wait gave up (as it must)
 };
 
 // --- TMA bulk copies and mbarriers (no cluster multicast anywhere) -----------

@@ -263,6 +263,12 @@ def device_error():
     return code.value
 
 
+def selftest_wait_timeout():
+    """Launch the library's wait-timeout self test (see w4a8.h); read the result
+    with device_error()."""
+    _lib.check(_lib.load().w4a8_selftest_wait_timeout(_stream()))
+
+
 def set_gemv_kernel(tensor_core):
     """Group-128 per-token GEMVs on the tensor-core kernel (True) or dp4a (False)."""
     _lib.load().w4a8_set_gemv_kernel(1 if tensor_core else 0)
