@@ -11,8 +11,9 @@ scales |N(0,1)|*0.01; activations fp32 N(0,1) quantized per token to int8.
           HBM, the 144 GEMV launches replayed as one CUDA graph with programmatic
           dependent launch between them;
   e2e     the same metric through the public API with host buffers: per step one
-          pinned-host -> device copy of the 144 fp32 input vectors, 144 quantize +
-          144 GEMV launches, one device -> host copy of all outputs;
+          pinned-host -> device copy of the 144 fp32 input vectors, 144 launches of
+          the GEMV with the per-token quant fused in (w4a8_gemv_x), one device ->
+          host copy of all outputs;
   extra   secondary BASELINE metrics from the same run: config 1 (single GEMV),
           config 3 (lm_head + fused argmax, tok/s), config 4 (prefill GEMM, TOPS),
           config 5 (batched GEMV, M = 2..16).
@@ -176,9 +177,6 @@ class Sweep:
         self.h_out = torch.empty(self.nout).pin_memory()
         self.d_in = torch.empty(self.nin, device=dev)
         self.d_out = torch.empty(self.nout, device=dev)
-        self.xq = torch.empty(max(ks), dtype=torch.int8, device=dev)
-        self.xq_all = [torch.empty((1, k), dtype=torch.int8, device=dev) for _ in range(LAYERS) for k, _ in SWEEP]
-        self.xs_all = [torch.empty(1, device=dev) for _ in range(LAYERS) for _ in SWEEP]
 
     def step(self):
         ops = self.ops
@@ -190,13 +188,13 @@ class Sweep:
     def step_e2e(self):
         ops = self.ops
         self.d_in.copy_(self.h_in, non_blocking=True)
-        i = o = j = 0
+        i = o = 0
         for layer in self.w:
             for (k, n), w in zip(SWEEP, layer):
                 x = self.d_in[i:i + k].view(1, k)
-                xq, xs = ops.quant(x, act=ops.ACT_TOKEN, xq=self.xq_all[j], xs=self.xs_all[j])
-                ops.gemv(w, xq, xs, act=ops.ACT_TOKEN, y=self.d_out[o:o + n].view(1, n))
-                i, o, j = i + k, o + n, j + 1
+                # per-token quant fused into the GEMV launch (w4a8_gemv_x)
+                ops.gemv_x(w, x, y=self.d_out[o:o + n].view(1, n))
+                i, o = i + k, o + n
         self.h_out.copy_(self.d_out, non_blocking=True)
 
     launches_per_step = LAYERS * len(SWEEP)
@@ -529,7 +527,7 @@ def main():
     try:
         ms_e2e, g2 = time_graph(torch, sweep.step_e2e, args.steps, args.warmup, sync_all)
         del g2
-        e2e_mode = "cuda graph of copy + quant + gemv"
+        e2e_mode = "cuda graph of H2D copy + fused quant/GEMV (w4a8_gemv_x) + D2H copy"
     except Exception as exc:  # capture of the host copies unsupported: time eagerly
         e2e_mode = f"eager ({type(exc).__name__})"
         for _ in range(args.warmup):

@@ -115,6 +115,16 @@ W4A8_API w4a8_status w4a8_quant(const float* x, const float* norm_w, float eps, 
 W4A8_API w4a8_status w4a8_gemv(const w4a8_weight* w, const int8_t* xq, const float* xs, int32_t act,
                       int32_t m, int32_t mode, float* y, void* stream);
 
+/* Per-token quantization and GEMV in one launch, for group-128 weights: the
+ * quant of a projection's input followed by the projection (Builder::quant then
+ * Builder::gemv, graph.rs:216-222 and 190-198; quant.wgsl with one scale per token,
+ * no norm, then gemv_q4q8.wgsl).  x f32[m, k] (16-byte aligned), m in
+ * [1, W4A8_GEMV_MAX_M]; y as w4a8_gemv.  The result is bit-identical to
+ * w4a8_quant(act = W4A8_ACT_TOKEN, norm_w = NULL) followed by w4a8_gemv.
+ * W4A8_ENOTSUP for other groups. */
+W4A8_API w4a8_status w4a8_gemv_x(const w4a8_weight* w, const float* x, int32_t m, int32_t mode, float* y,
+                                 void* stream);
+
 /* Prefill GEMM Y[m, n] = X W^T for any m >= 1 (gemm_q4q8.wgsl:46-121,
  * Builder::gemm graph.rs:200-205).  Group-128 symmetric weights with
  * W4A8_ACT_TOKEN run on the tcgen05 tensor cores (int4 expanded to int8 in shared

@@ -289,3 +289,38 @@ def test_tensor_core_and_dp4a_kernels_agree(cuda, has_min, m, mode, nk):
     ops.set_gemv_kernel(True)
     np.testing.assert_array_equal(bits(outs[0]), bits(outs[1]))
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("has_min", [False, True])
+@pytest.mark.parametrize("nk", [(96, 2048), (64, 6144), (40, 128)])
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 9, 16])
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_gemv_fused_quant_bit_exact(cuda, has_min, nk, m, mode):
+    """w4a8_gemv_x (per-token quant inside the GEMV) equals w4a8_quant + w4a8_gemv and
+    the oracle bit for bit, zero rows included."""
+    n, k = nk
+    q, s, _ = make_weight(n, k, 128, has_min, seed=n + k + m)
+    x = make_x(m, k, seed=m + 17)
+    if m > 2:
+        x[1] = 0.0  # a zero row: dx = 0, all codes 0
+    xq, xs = orc.quant(x, act=1)
+    n_out = n // 2 if mode == 2 else n
+    y0 = make_x(m, n_out, seed=5) if mode == 1 else None
+    ref = orc.gemv(q, s, k, 128, has_min, xq, xs, act=1, mode=mode, y=None if y0 is None else y0.copy())
+    w = dev_weight(q, s, n, k, 128, has_min, cuda)
+    y = ops.gemv_x(w, to_dev(x, cuda), mode=mode, y=None if y0 is None else to_dev(y0, cuda))
+    xq_d, xs_d = ops.quant(to_dev(x, cuda), act=1)
+    y2 = ops.gemv(w, xq_d, xs_d, act=1, mode=mode, y=None if y0 is None else to_dev(y0, cuda))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(bits(y.cpu().numpy()), bits(y2.cpu().numpy()))
+    if mode == 2:
+        assert_rel_close(y.cpu().numpy(), ref, 1e-3)
+    else:
+        np.testing.assert_array_equal(bits(y.cpu().numpy()), bits(ref))
+
+
+def test_gemv_fused_quant_rejects_group32(cuda):
+    q, s, _ = make_weight(32, 256, 32, True, seed=1)
+    w = dev_weight(q, s, 32, 256, 32, True, cuda)
+    with pytest.raises(W4A8Error):
+        ops.gemv_x(w, to_dev(make_x(1, 256), cuda))

@@ -169,6 +169,27 @@ w4a8_status w4a8_gemv(const w4a8_weight* w, const int8_t* xq, const float* xs, i
     return launch_gemv(p, w->group, w->has_min != 0, act, mode, OUT_Y, static_cast<cudaStream_t>(stream));
 }
 
+w4a8_status w4a8_gemv_x(const w4a8_weight* w, const float* x, int32_t m, int32_t mode, float* y, void* stream) {
+    w4a8_status st = check_weight(w, "w4a8_gemv_x");
+    if (st != W4A8_OK) return st;
+    if (w->group != 128) return set_error(W4A8_ENOTSUP, "w4a8_gemv_x: group-128 weights only (group %d)", w->group);
+    if (!x || !aligned(x, 16)) return set_error(W4A8_EINVAL, "w4a8_gemv_x: x NULL or not 16-byte aligned");
+    if (!y) return set_error(W4A8_EINVAL, "w4a8_gemv_x: y is NULL");
+    if (m < 1 || m > W4A8_GEMV_MAX_M) return set_error(W4A8_EINVAL, "w4a8_gemv_x: m=%d not in [1, %d]", m, W4A8_GEMV_MAX_M);
+    if (mode < W4A8_STORE || mode > W4A8_SWIGLU) return set_error(W4A8_EINVAL, "w4a8_gemv_x: mode=%d", mode);
+    if (mode == W4A8_SWIGLU && w->n % 2) return set_error(W4A8_EINVAL, "w4a8_gemv_x: SWIGLU needs even n (%d)", w->n);
+    GemvParams p{};
+    p.q = static_cast<const uint4*>(w->q);
+    p.s = w->s;
+    p.xf32 = x;
+    p.y = y;
+    p.n_out = mode == W4A8_SWIGLU ? w->n / 2 : w->n;
+    p.y_stride = p.n_out;
+    p.k = w->k;
+    p.m = m;
+    return launch_gemv_mma(p, w->has_min != 0, mode, OUT_Y, static_cast<cudaStream_t>(stream));
+}
+
 w4a8_status w4a8_group_dots(const w4a8_weight* w, const int8_t* xq, int32_t m, int32_t* dots, void* stream) {
     w4a8_status st = check_weight(w, "w4a8_group_dots");
     if (st != W4A8_OK) return st;

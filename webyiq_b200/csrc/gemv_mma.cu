@@ -10,10 +10,10 @@ namespace {
 
 // One CTA per SM (fewer when rows are scarce) on balanced row ranges; a round is
 // RT tiles of 16 rows (8 output rows for SWIGLU); RT x KS warps, KS = ceil(KG/4).
-template <bool HAS_MIN, int MODE, int OUT, int MT>
+template <bool HAS_MIN, int MODE, int OUT, int MT, bool FQ>
 w4a8_status launch_mt(MmaParams p, cudaStream_t st) {
     static size_t configured = 48 * 1024;
-    auto kernel = gemv_mma_kernel<HAS_MIN, MODE, OUT, MT>;
+    auto kernel = gemv_mma_kernel<HAS_MIN, MODE, OUT, MT, FQ>;
     const int kg = p.k / 128;
     p.ks = (kg + kMmaGPS - 1) / kMmaGPS;
     if (p.ks > kMmaMaxWarps) return set_error(W4A8_EINVAL, "w4a8 gemv: k=%d too large", p.k);
@@ -43,16 +43,21 @@ w4a8_status launch_mt(MmaParams p, cudaStream_t st) {
     return launch_pdl("w4a8 gemv (mma)", kernel, dim3(ctas), dim3(p.rt * p.ks * 32), plan.total, st, p);
 }
 
-template <bool HAS_MIN, int MODE, int OUT>
+template <bool HAS_MIN, int MODE, int OUT, bool FQ = false>
 w4a8_status launch_one(const MmaParams& p, cudaStream_t st) {
-    if (p.m <= 1) return launch_mt<HAS_MIN, MODE, OUT, 1>(p, st);
-    if (p.m <= 2) return launch_mt<HAS_MIN, MODE, OUT, 2>(p, st);
-    if (p.m <= 4) return launch_mt<HAS_MIN, MODE, OUT, 4>(p, st);
-    return launch_mt<HAS_MIN, MODE, OUT, 8>(p, st);
+    if (p.m <= 1) return launch_mt<HAS_MIN, MODE, OUT, 1, FQ>(p, st);
+    if (p.m <= 2) return launch_mt<HAS_MIN, MODE, OUT, 2, FQ>(p, st);
+    if (p.m <= 4) return launch_mt<HAS_MIN, MODE, OUT, 4, FQ>(p, st);
+    return launch_mt<HAS_MIN, MODE, OUT, 8, FQ>(p, st);
 }
 
 template <bool HAS_MIN>
 w4a8_status launch_mode(const MmaParams& p, int mode, int out, cudaStream_t st) {
+    if (p.xf32) {  // f32 activations, quantized inside (OUT_Y only)
+        if (mode == W4A8_STORE) return launch_one<HAS_MIN, W4A8_STORE, OUT_Y, true>(p, st);
+        if (mode == W4A8_ADD) return launch_one<HAS_MIN, W4A8_ADD, OUT_Y, true>(p, st);
+        return launch_one<HAS_MIN, W4A8_SWIGLU, OUT_Y, true>(p, st);
+    }
     if (out == OUT_DOTS) return launch_one<HAS_MIN, W4A8_STORE, OUT_DOTS>(p, st);
     if (out == OUT_ARGMAX) return launch_one<HAS_MIN, W4A8_STORE, OUT_ARGMAX>(p, st);
     if (mode == W4A8_STORE) return launch_one<HAS_MIN, W4A8_STORE, OUT_Y>(p, st);
@@ -70,7 +75,8 @@ w4a8_status launch_gemv_mma(const GemvParams& g, bool has_min, int mode, int out
         p.q = g.q;
         p.s = g.s;
         p.m = g.m - t0 < kMmaTokens ? g.m - t0 : kMmaTokens;
-        p.xq = g.xq + static_cast<size_t>(t0) * g.k;
+        p.xq = g.xq ? g.xq + static_cast<size_t>(t0) * g.k : nullptr;
+        p.xf32 = g.xf32 ? g.xf32 + static_cast<size_t>(t0) * g.k : nullptr;
         p.xs = g.xs ? g.xs + t0 : nullptr;
         p.y = g.y ? g.y + static_cast<size_t>(t0) * g.y_stride : nullptr;
         p.dots = g.dots ? g.dots + static_cast<size_t>(t0) * g.n_out * kg : nullptr;

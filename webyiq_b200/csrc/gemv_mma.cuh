@@ -50,6 +50,7 @@ struct MmaParams {
     const void* s;         // scales: u16 f16 (symmetric) or u32 (scale, min)
     const int8_t* xq;      // [m, k]
     const float* xs;       // [m] per-token dx
+    const float* xf32;     // [m, k] f32 activations to quantize here (xq, xs unused), or null
     float* y;              // OUT_Y output; OUT_ARGMAX logits or null
     int* dots;             // OUT_DOTS [m, n_out, k/128]
     unsigned int* counter;
@@ -113,7 +114,8 @@ struct MmaBounds {
     static constexpr int min_blocks = MT == 1 ? 2 : 1;
 };
 
-template <bool HAS_MIN, int MODE, int OUT, int MT>
+// FQ: the activations arrive as f32 (p.xf32) and are quantized per token here.
+template <bool HAS_MIN, int MODE, int OUT, int MT, bool FQ>
 __global__ void __launch_bounds__(kMmaMaxWarps * 32, MmaBounds<MT>::min_blocks)
 gemv_mma_kernel(const MmaParams p) {
     constexpr bool SWI = (MODE == W4A8_SWIGLU);
@@ -215,6 +217,11 @@ gemv_mma_kernel(const MmaParams p) {
         }
     };
 
+    // Fused quant: per-token absmax, as float bits (non-negative, so they order
+    // as unsigned integers), filled by shared-memory atomicMax.
+    __shared__ unsigned int s_amax_bits[kMmaTokens];
+    if (FQ && tid < kMmaTokens) s_amax_bits[tid] = 0u;
+
     // Weights first: they do not depend on the previous kernel.
     if (warp == 0) {
         if (lane == 0) {
@@ -230,12 +237,99 @@ gemv_mma_kernel(const MmaParams p) {
     pdl_wait();  // activations (and y for ADD) come from the previous kernel
 
     load_scales(0);
-    if (OUT != OUT_DOTS && tid < m) sdx[tid] = __ldg(p.xs + tid);  // the dots hook has no xs
     // Activation operands and group sums.  Work item (g, t, tq): the 32 bytes
     // x[t][128g + 32tq ..] that lane-quarter tq of the mma meets, stored as
     // [g][t][tq][8 words]; the quarter sums of a group are added by shuffles
     // (items of one (g, t) are 4 neighbouring threads).
-    {
+    if (FQ) {
+        // Per-token quantization fused in (quant.wgsl with one scale per token):
+        // amax over the row, dx = amax / 127, inv = 1 / dx (0 for a zero row) and
+        // rint(x * inv), exactly as w4a8_quant computes them, so the result equals
+        // w4a8_quant followed by this GEMV bit for bit.  Every CTA quantizes the
+        // rows it needs (they come from L2).  When every work item has a thread
+        // (the decode case), the item's 32 inputs stay in registers across the
+        // absmax exchange: one pass over x.
+        __syncthreads();  // s_amax_bits zeroed
+        const int nitem = KG * m * 4;
+        // 32 inputs of item i -> int8 words in xf, their sum returned
+        auto put = [&](int i, const float (&e)[32], float inv) -> int {
+            int X = 0;
+            uint32_t wd[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const int q0 = static_cast<int>(rintf(__fmul_rn(e[4 * c], inv)));
+                const int q1 = static_cast<int>(rintf(__fmul_rn(e[4 * c + 1], inv)));
+                const int q2 = static_cast<int>(rintf(__fmul_rn(e[4 * c + 2], inv)));
+                const int q3 = static_cast<int>(rintf(__fmul_rn(e[4 * c + 3], inv)));
+                X += q0 + q1 + q2 + q3;
+                wd[c] = (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
+                        ((static_cast<uint32_t>(q2) & 0xffu) << 16) | ((static_cast<uint32_t>(q3) & 0xffu) << 24);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(xf + static_cast<size_t>(i) * 8);
+            dst[0] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+            dst[1] = make_uint4(wd[4], wd[5], wd[6], wd[7]);
+            return X;
+        };
+        auto load = [&](int i, float (&e)[32]) -> int {  // returns the item's token
+            const int tq2 = i & 3, t = (i >> 2) % m, g = (i >> 2) / m;
+            const float4* src =
+                reinterpret_cast<const float4*>(p.xf32 + static_cast<size_t>(t) * p.k + g * 128 + tq2 * 32);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const float4 v = __ldg(src + c);
+                e[4 * c] = v.x;
+                e[4 * c + 1] = v.y;
+                e[4 * c + 2] = v.z;
+                e[4 * c + 3] = v.w;
+            }
+            return t;
+        };
+        auto local_max = [](const float (&e)[32]) -> float {
+            float a = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) a = fmaxf(a, fabsf(e[c]));
+            return a;
+        };
+        auto inv_of = [&](int t) -> float {
+            const float a = __uint_as_float(s_amax_bits[t]);
+            return a > 0.0f ? __fdiv_rn(1.0f, __fdiv_rn(a, 127.0f)) : 0.0f;
+        };
+        if (nitem <= static_cast<int>(blockDim.x)) {
+            float e[32];
+            int t = 0;
+            if (tid < nitem) {
+                t = load(tid, e);
+                atomicMax(&s_amax_bits[t], __float_as_uint(local_max(e)));
+            }
+            __syncthreads();
+            int X = 0;
+            if (tid < nitem) X = put(tid, e, inv_of(t));
+            X += __shfl_xor_sync(kFull, X, 1);
+            X += __shfl_xor_sync(kFull, X, 2);
+            if (tid < nitem && (tid & 3) == 0) xg[tid >> 2] = X;  // [g][t]
+        } else {
+            for (int i = tid; i < nitem; i += blockDim.x) {
+                float e[32];
+                const int t = load(i, e);
+                atomicMax(&s_amax_bits[t], __float_as_uint(local_max(e)));
+            }
+            __syncthreads();
+            for (int i0 = 0; i0 < nitem; i0 += blockDim.x) {
+                const int i = i0 + tid;
+                int X = 0;
+                if (i < nitem) {
+                    float e[32];
+                    const int t = load(i, e);
+                    X = put(i, e, inv_of(t));
+                }
+                X += __shfl_xor_sync(kFull, X, 1);
+                X += __shfl_xor_sync(kFull, X, 2);
+                if (i < nitem && (i & 3) == 0) xg[i >> 2] = X;  // [g][t]
+            }
+        }
+        if (OUT != OUT_DOTS && tid < m) sdx[tid] = __fdiv_rn(__uint_as_float(s_amax_bits[tid]), 127.0f);
+    } else {
+        if (OUT != OUT_DOTS && tid < m) sdx[tid] = __ldg(p.xs + tid);  // the dots hook has no xs
         const int nitem = KG * m * 4;
         for (int i0 = 0; i0 < nitem; i0 += blockDim.x) {
             const int i = i0 + tid;

@@ -84,6 +84,16 @@ def gemv(w, xq, xs, act=ACT_GROUP32, mode=STORE, y=None):
     return y
 
 
+def gemv_x(w, x, mode=STORE, y=None):
+    """Per-token quant of f32 x [m, k] and the GEMV in one launch (group-128 weights);
+    equal to quant(act=ACT_TOKEN) followed by gemv, bit for bit."""
+    _need_cuda(x, y)
+    m = x.shape[0]
+    y = _out(w, m, mode, y, x.device)
+    _lib.check(_lib.load().w4a8_gemv_x(ctypes.byref(w.c), _ptr(x), m, mode, _ptr(y), _stream()))
+    return y
+
+
 def gemm(w, xq, xs, act=ACT_GROUP32, mode=STORE, y=None):
     """Y (+)= X W^T for any m (gemm_q4q8.wgsl)."""
     _need_cuda(xq, xs, y)
