@@ -186,6 +186,36 @@ def test_lmhead_argmax_exact(cuda, m):
     np.testing.assert_array_equal(tok.cpu().numpy().astype(np.uint32), ids[ref_tok])
 
 
+@pytest.mark.parametrize("has_min", [False, True])
+@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("n,k", [(296, 1024), (9472, 384), (19000, 2048), (148 * 64 * 3 + 40, 2048),
+                                 (12344, 2560), (10008, 4096), (4840, 8192)])
+def test_lmhead_stream_shapes(cuda, n, k, m, has_min):
+    """The streaming lm_head (group 128, per-token, one or two tokens, n a multiple
+    of 8) over each split of a row between lanes (8, 16 or 32 lanes of one or two
+    groups, idle lanes past the row's end), ragged last stages and CTAs of a single
+    8-row block; k=8192 with two tokens is past its cover and takes the other
+    kernel.  Logits bit-exact, the argmax with a planted tie."""
+    q, s, _ = make_weight(n, k, 128, has_min, seed=k + n)
+    xq, xs = orc.quant(make_x(m, k, seed=k), act=1)
+    logits = orc.gemv(q, s, k, 128, has_min, xq, xs, act=1)
+    best = int(orc.argmax(logits)[0])
+    lo = best // 3  # a copy of the best row at a lower index wins the tie
+    q[lo], s[lo] = q[best], s[best]
+    logits = orc.gemv(q, s, k, 128, has_min, xq, xs, act=1)
+    ref = orc.argmax(logits)
+    assert ref[0] == min(lo, best)
+    w = dev_weight(q, s, n, k, 128, has_min, cuda)
+    lg = torch.empty((m, n), dtype=torch.float32, device=cuda)
+    ws = ops.lmhead_workspace(w, m, cuda)
+    for _ in range(2):
+        key, tok = ops.lmhead_argmax(w, to_dev(xq, cuda), to_dev(xs, cuda), act=1, logits=lg, workspace=ws)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(bits(lg.cpu().numpy()), bits(logits))
+        np.testing.assert_array_equal(tok.cpu().numpy().astype(np.uint32), ref)
+    assert ops.device_error() == 0
+
+
 @pytest.mark.parametrize("shards", [2, 4, 8])
 def test_lmhead_sharded_merge(cuda, shards):
     """Column split with row_offset: the max of the shard keys is the full key."""

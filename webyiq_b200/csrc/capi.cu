@@ -57,6 +57,8 @@ w4a8_status launch_quant(const float*, const float*, float, int, int, int, int8_
 w4a8_status launch_argmax(const float*, int, int, const uint32_t*, uint32_t*, cudaStream_t);
 
 w4a8_status launch_gemv_mma(const GemvParams& g, bool has_min, int mode, int out, cudaStream_t st);
+bool lmhead_stream_covers(const GemvParams& g, int group, int act);
+w4a8_status launch_lmhead_stream(const GemvParams& g, bool has_min, cudaStream_t st);
 w4a8_status device_error(unsigned int* code, cudaStream_t st);
 w4a8_status selftest_wait_timeout(cudaStream_t st);
 w4a8_status launch_gemm_tc(const w4a8_weight* w, const int8_t* xq, const float* dx, int m, int mode, float* y,
@@ -70,7 +72,11 @@ bool tc_gemm_format(const w4a8_weight* w, int act) {
 // Group-128 weights with per-token activations go to the tensor-core GEMV;
 // everything else (the engine's group-32 format, per-32 activations) to the dp4a one.
 w4a8_status launch_gemv(const GemvParams& p, int group, bool has_min, int act, int mode, int out, cudaStream_t st) {
-    // (the lm_head argmax stays on the dp4a kernel: measured faster for vocabulary-sized n)
+    // The group-128 per-token lm_head argmax streams the vocabulary through its own
+    // kernel (lmhead_stream.cu); the tensor-core GEMV takes the other group-128
+    // per-token calls, the dp4a GEMV everything else.
+    if (out == OUT_ARGMAX && g_use_mma && lmhead_stream_covers(p, group, act))
+        return launch_lmhead_stream(p, has_min, st);
     if (group == 128 && (act == W4A8_ACT_TOKEN || out == OUT_DOTS) && out != OUT_ARGMAX && g_use_mma)
         return launch_gemv_mma(p, has_min, mode, out, st);
     if (group == 32) return has_min ? launch_gemv_g32_m1(p, act, mode, out, st) : launch_gemv_g32_m0(p, act, mode, out, st);
