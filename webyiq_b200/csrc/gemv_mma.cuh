@@ -79,7 +79,7 @@ __host__ __device__ inline int mma_row_stride(int k) {
 // Shared memory: weight stages [S][rt*16 rows][stride], their scales
 // [S][rt*16 rows][k/128] (rows in the order they are copied), activation operands
 // [KG][m][4][8 words] (the 32 bytes lane-quarter t meets), per-group activation
-// sums [KG][m], K-slice partial sums [rt][ks][16][8] (int64), one mbarrier per stage.
+// sums [KG][m], K-slice partial sums [rt][ks][16][8] (int64).
 struct MmaSmem {
     size_t stage, stage_bytes, sc, sc_bytes, xf, xg, dx, red, bar, total;
 };
@@ -134,6 +134,14 @@ gemv_mma_kernel(const MmaParams p) {
     const int g1 = static_cast<int>(static_cast<long long>(slice + 1) * KG / ks);
     const int ng = g1 - g0;  // <= kMmaGPS (host guarantees)
     const int stride = mma_row_stride(p.k);
+    // B column c carries token c % MT of the groups in slot c / CW (zeros for the
+    // other groups), so the D registers of lane (gq, tq) accumulate ONE group per
+    // accumulator set and the lanes of a quad share the per-group scale steps.
+    constexpr int CW = MT >= 2 ? MT : 2;   // B columns per slot
+    constexpr int NSLOT = 8 / CW;          // slots = groups per accumulator set (4, 4, 2, 1)
+    constexpr int NSET = kMmaGPS / NSLOT;  // accumulator sets (1, 1, 2, 4)
+    const int bslot = gq / CW, btok = gq % MT;  // B column gq
+    const int dslot = (2 * tq) / CW;            // D columns 2tq, 2tq+1
     const int sb = HAS_MIN ? 4 : 2;
     const MmaSmem sp = mma_smem_plan(m, p.k, rt, ks, S, sb);
     // scales travel with the weights when a row of them is a whole number of
@@ -143,42 +151,45 @@ gemv_mma_kernel(const MmaParams p) {
     uint32_t* xf = reinterpret_cast<uint32_t*>(smem + sp.xf);
     int* xg = reinterpret_cast<int*>(smem + sp.xg);
     long long* red = reinterpret_cast<long long*>(smem + sp.red);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + sp.bar);
 
     const int rb = static_cast<int>(static_cast<long long>(blockIdx.x) * p.n_out / gridDim.x);
     const int re = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * p.n_out / gridDim.x);
     const int rows_round = rt * TR;
     const int rounds = (re - rb + rows_round - 1) / rows_round;
 
-    // Warp 0 requests round r into stage `slot`: one bulk copy per weight row into
-    // its padded shared-memory row (A rows 0-7 gate / 8-15 up for SWIGLU).
+    // Every thread copies 16-byte pieces of round r into stage `slot` as one commit
+    // group (cp.async: copies issued before griddepcontrol.wait then land while the
+    // previous kernel still runs); a warp takes whole rows into their padded
+    // shared-memory rows (A rows 0-7 gate / 8-15 up for SWIGLU).
     auto issue = [&](int r, int slot) {
         const int o0 = rb + r * rows_round;
         const int nrow = min(rows_round, re - o0);
         const int ncopy = (SWI ? 2 : 1) * nrow;
-        const uint32_t row_bytes = static_cast<uint32_t>(p.k / 2);
-        const uint32_t srow_bytes = static_cast<uint32_t>(KG * sb);
-        if (lane == 0) {
-            mbar_expect_tx(&bar[slot], static_cast<uint32_t>(ncopy) * (row_bytes + (scale_tma ? srow_bytes : 0u)));
-            if (scale_tma) {  // [h][row][KG]: gate (or all) rows, then up rows
-                unsigned char* sdst = smem + sp.sc + static_cast<size_t>(slot) * sp.sc_bytes;
-                for (int h = 0; h < (SWI ? 2 : 1); ++h)
-                    tma_bulk_load(sdst + static_cast<size_t>(h) * rows_round * srow_bytes,
-                                  static_cast<const unsigned char*>(p.s) +
-                                      (static_cast<size_t>(o0) + static_cast<size_t>(h) * p.n_out) * srow_bytes,
-                                  static_cast<uint32_t>(nrow) * srow_bytes, &bar[slot]);
-            }
-        }
-        __syncwarp();
+        const int nwarps = static_cast<int>(blockDim.x >> 5);
         unsigned char* st = smem + sp.stage + static_cast<size_t>(slot) * sp.stage_bytes;
-        for (int i = lane; i < ncopy; i += 32) {
+        for (int i = warp; i < ncopy; i += nwarps) {
             const int h = SWI ? (i >= nrow) : 0;
             const int ri = i - h * nrow;
             const int srow = SWI ? (ri / 8) * 16 + (ri % 8) + 8 * h : ri;
             const uint4* src = p.q + (static_cast<size_t>(o0 + ri) + static_cast<size_t>(h) * p.n_out) * KC;
-            tma_bulk_load(st + static_cast<size_t>(srow) * stride, src, row_bytes, &bar[slot]);
+            unsigned char* dst = st + static_cast<size_t>(srow) * stride;
+            for (int c = lane; c < KC; c += 32) cp_async16(dst + c * 16, src + c);
         }
+        if (scale_tma) {  // [h][row][KG]: gate (or all) rows, then up rows
+            const int srow_bytes = KG * sb, pieces = nrow * srow_bytes / 16;
+            unsigned char* sdst = smem + sp.sc + static_cast<size_t>(slot) * sp.sc_bytes;
+            for (int h = 0; h < (SWI ? 2 : 1); ++h) {
+                const uint4* ssrc = reinterpret_cast<const uint4*>(
+                    static_cast<const unsigned char*>(p.s) +
+                    (static_cast<size_t>(o0) + static_cast<size_t>(h) * p.n_out) * srow_bytes);
+                uint4* d = reinterpret_cast<uint4*>(sdst + static_cast<size_t>(h) * rows_round * srow_bytes);
+                for (int i = tid; i < pieces; i += blockDim.x) cp_async16(d + i, ssrc + i);
+            }
+        }
+        cp_async_commit();
     };
+    // this thread's pieces of round r have landed (rounds up to r + S - 1 are issued)
+    auto wait_round = [&](int r) { cp_async_wait_upto(min(r + S - 1, rounds - 1) - r); };
     auto prefetch_scales = [&](int r) {  // the fallback: the round's scale span towards L2
         if (scale_tma || tid != 0 || r >= rounds) return;
         const int o0 = rb + r * rows_round, o1 = min(o0 + rows_round, re);
@@ -198,21 +209,24 @@ gemv_mma_kernel(const MmaParams p) {
         oka = active && t0 + gq < re;
         okc = active && (SWI ? t0 + gq < re : t0 + gq + 8 < re);
     };
-    uint32_t sa[kMmaGPS], sc[kMmaGPS];
+    uint32_t sa[NSET], sc[NSET];  // scales of this lane's groups (set a: group a * NSLOT + dslot)
     auto load_scales = [&](int r) {  // the fallback when scales are not staged by TMA
         if (scale_tma) return;
         int ra, rc;
         bool oka, okc;
         lane_rows(r, ra, rc, oka, okc);
 #pragma unroll
-        for (int j = 0; j < kMmaGPS; ++j) {
+        for (int a = 0; a < NSET; ++a) {
+            const int j = a * NSLOT + dslot;
             const size_t ea = static_cast<size_t>(ra) * KG + g0 + j, ec = static_cast<size_t>(rc) * KG + g0 + j;
-            sa[j] = sc[j] = 0u;
+            uint32_t& sj = sa[a];
+            uint32_t& cj = sc[a];
+            sj = cj = 0u;
             if (j < ng && oka)
-                sa[j] = HAS_MIN ? __ldg(static_cast<const uint32_t*>(p.s) + ea)
+                sj = HAS_MIN ? __ldg(static_cast<const uint32_t*>(p.s) + ea)
                                 : static_cast<uint32_t>(__ldg(static_cast<const unsigned short*>(p.s) + ea));
             if (j < ng && okc)
-                sc[j] = HAS_MIN ? __ldg(static_cast<const uint32_t*>(p.s) + ec)
+                cj = HAS_MIN ? __ldg(static_cast<const uint32_t*>(p.s) + ec)
                                 : static_cast<uint32_t>(__ldg(static_cast<const unsigned short*>(p.s) + ec));
         }
     };
@@ -220,17 +234,14 @@ gemv_mma_kernel(const MmaParams p) {
     // Fused quant: per-token absmax, as float bits (non-negative, so they order
     // as unsigned integers), filled by shared-memory atomicMax.
     __shared__ unsigned int s_amax_bits[kMmaTokens];
+    __shared__ uint4 s_xzero[2];  // the activations a B column meets outside its slot
+    if (tid < 2) s_xzero[tid] = make_uint4(0, 0, 0, 0);
     if (FQ && tid < kMmaTokens) s_amax_bits[tid] = 0u;
 
-    // Weights first: they do not depend on the previous kernel.
-    if (warp == 0) {
-        if (lane == 0) {
-            for (int s2 = 0; s2 < S; ++s2) mbar_init(&bar[s2], 1);
-            mbar_init_fence();
-        }
-        __syncwarp();
-        for (int r = 0; r < S && r < rounds; ++r) issue(r, r);
-    }
+    // Weights first: they do not depend on the previous kernel.  Each thread waits
+    // for its own pieces of round 0 before the dependency wait.
+    for (int r = 0; r < S && r < rounds; ++r) issue(r, r);
+    if (rounds > 0) wait_round(0);
     prefetch_scales(0);
     prefetch_scales(1);
     pdl_launch_dependents();
@@ -356,11 +367,9 @@ gemv_mma_kernel(const MmaParams p) {
 
     for (int r = 0; r < rounds; ++r) {
         const int slot = r % S;
-        // one thread waits for the copies; the barrier releases (and orders) the rest
-        const bool ok_wait = tid != 0 || mbar_wait(&bar[slot], static_cast<uint32_t>((r / S) & 1));
-        if (__syncthreads_or(!ok_wait)) {  // a copy never landed: report, do not hang
-            if (tid == 0) atomicOr(&g_w4a8_dev_error, DEV_ERR_TMA_TIMEOUT);
-            return;
+        if (r > 0) {  // round 0 landed before the dependency wait
+            wait_round(r);
+            __syncthreads();
         }
         prefetch_scales(r + 2);
         int ra, rc;
@@ -373,7 +382,16 @@ gemv_mma_kernel(const MmaParams p) {
         const int ric = SWI ? rows_round + ria : ria + 8;
         const unsigned char* rowa = st + static_cast<size_t>(tile * 16 + gq) * stride + tq * 16;
         const unsigned char* rowc = rowa + static_cast<size_t>(8) * stride;
-        long long acc[4] = {0, 0, 0, 0};  // [row gq | gq+8][token 2tq | 2tq+1]
+        // two accumulators per set (by group parity) when a set takes several
+        // groups, so that the dependent mma chains stay short
+        constexpr int NSUB = NSLOT > 1 ? 2 : 1;
+        int dl[NSET][NSUB][4], dh[NSET][NSUB][4];
+#pragma unroll
+        for (int a = 0; a < NSET; ++a)
+#pragma unroll
+            for (int u = 0; u < NSUB; ++u)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) dl[a][u][e] = dh[a][u][e] = 0;
 #pragma unroll
         for (int j = 0; j < kMmaGPS; ++j) {
             if (j >= ng) break;
@@ -383,26 +401,41 @@ gemv_mma_kernel(const MmaParams p) {
                 wa = *reinterpret_cast<const uint4*>(rowa + g * 64);
                 wc = *reinterpret_cast<const uint4*>(rowc + g * 64);
             }
-            uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
-            if (gq < m) {  // B column gq = token gq (lanes 4t..4t+3)
-                const uint4* xp = reinterpret_cast<const uint4*>(xf + ((static_cast<size_t>(g) * m + gq) * 4 + tq) * 8);
-                x0 = xp[0];  // activations of k-words 0, 1 (low 4, high 4 each)
-                x1 = xp[1];  // k-words 2, 3
-            }
+            // B column gq: token btok's activations if group j is in its slot
+            const bool mine = (j % NSLOT) == bslot && btok < m;
+            const uint4* xp = mine ? reinterpret_cast<const uint4*>(xf + ((static_cast<size_t>(g) * m + btok) * 4 + tq) * 8)
+                                   : s_xzero;
+            const uint4 x0 = xp[0];  // activations of k-words 0, 1 (low 4, high 4 each)
+            const uint4 x1 = xp[1];  // k-words 2, 3
             const uint32_t ml = 0x0F0F0F0Fu, mh = 0xF0F0F0F0u;
-            int dl[4] = {0, 0, 0, 0}, dh[4] = {0, 0, 0, 0};
+            int (&sl)[4] = dl[j / NSLOT][j % NSUB];
+            int (&sh)[4] = dh[j / NSLOT][j % NSUB];
             // k-words w0, w1 of rows gq (wa) and gq+8 (wc); A k-slots 0-3 / 16-19
             // of this lane meet B words 0 / 1 of the same lane
-            mma_u8s8(dl, wa.x & ml, wc.x & ml, wa.y & ml, wc.y & ml, x0.x, x0.z);
-            mma_u8s8(dl, wa.z & ml, wc.z & ml, wa.w & ml, wc.w & ml, x1.x, x1.z);
-            mma_u8s8(dh, wa.x & mh, wc.x & mh, wa.y & mh, wc.y & mh, x0.y, x0.w);
-            mma_u8s8(dh, wa.z & mh, wc.z & mh, wa.w & mh, wc.w & mh, x1.y, x1.w);
-            // element e: A row gq (e < 2) or gq+8, token 2tq + (e & 1)
+            mma_u8s8(sl, wa.x & ml, wc.x & ml, wa.y & ml, wc.y & ml, x0.x, x0.z);
+            mma_u8s8(sl, wa.z & ml, wc.z & ml, wa.w & ml, wc.w & ml, x1.x, x1.z);
+            mma_u8s8(sh, wa.x & mh, wc.x & mh, wa.y & mh, wc.y & mh, x0.y, x0.w);
+            mma_u8s8(sh, wa.z & mh, wc.z & mh, wa.w & mh, wc.w & mh, x1.y, x1.w);
+        }
+        // the exact per-group scale step of this lane's groups; element e: A row gq
+        // (e < 2) or gq+8, D column 2tq + (e & 1) = token (2tq + (e & 1)) % MT
+        long long acc[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int a = 0; a < NSET; ++a) {
+            const int j = a * NSLOT + dslot;
+            if (j >= ng) continue;
+            const int g = g0 + j;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const int t = 2 * tq + (e & 1);
-                if ((e & 1) >= MT || t >= m) continue;
-                const int I = dl[e] + (dh[e] >> 4);  // dh = 16 * high-nibble dot, exact
+                if (MT == 1 && (e & 1)) continue;  // both D columns hold token 0
+                const int t = MT == 1 ? 0 : (2 * tq + (e & 1)) % MT;
+                if (t >= m) continue;
+                int lo = dl[a][0][e], hi = dh[a][0][e];
+                if (NSUB == 2) {
+                    lo += dl[a][NSUB - 1][e];
+                    hi += dh[a][NSUB - 1][e];
+                }
+                const int I = lo + (hi >> 4);  // hi = 16 * high-nibble dot, exact
                 const int X = xg[g * m + t];
                 uint32_t s;
                 if (scale_tma) {
@@ -410,7 +443,7 @@ gemv_mma_kernel(const MmaParams p) {
                     s = HAS_MIN ? reinterpret_cast<const uint32_t*>(scs)[si]
                                 : static_cast<uint32_t>(reinterpret_cast<const unsigned short*>(scs)[si]);
                 } else {
-                    s = e < 2 ? sa[j] : sc[j];
+                    s = e < 2 ? sa[a] : sc[a];
                 }
                 if (OUT == OUT_DOTS) {
                     const bool ok = e < 2 ? oka : okc;
@@ -425,20 +458,28 @@ gemv_mma_kernel(const MmaParams p) {
                 }
             }
         }
-        if (r + 1 < rounds) load_scales(r + 1);  // in flight during the sums below
-        if (OUT != OUT_DOTS && active) {  // K-slice partial sums: red[tile][slice][A row][token]
+        // lanes of a quad holding the same rows and tokens (other groups) add up
+        if (OUT != OUT_DOTS && MT <= 4) {
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const int t = 2 * tq + (e & 1);
+                if (MT == 1 && (e & 1)) continue;
+                if (MT <= 2) acc[e] += shfl_xor_i64(acc[e], 1);
+                acc[e] += shfl_xor_i64(acc[e], 2);
+            }
+        }
+        if (r + 1 < rounds) load_scales(r + 1);  // in flight during the sums below
+        const bool writer = MT <= 2 ? tq == 0 : (MT == 4 ? tq < 2 : true);
+        if (OUT != OUT_DOTS && active && writer) {  // K-slice partial sums: red[tile][slice][A row][token]
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                if (MT == 1 && (e & 1)) continue;
+                const int t = MT == 1 ? 0 : (2 * tq + (e & 1)) % MT;
                 const int arow = gq + (e >= 2 ? 8 : 0);
-                if ((e & 1) < MT && t < m) red[((static_cast<size_t>(tile) * ks + slice) * 16 + arow) * kMmaTokens + t] = acc[e];
+                if (t < m) red[((static_cast<size_t>(tile) * ks + slice) * 16 + arow) * kMmaTokens + t] = acc[e];
             }
         }
         __syncthreads();  // every warp is done with stage `slot` and has stored its sums
-        if (warp == 0 && r + S < rounds) {
-            fence_proxy_async();
-            issue(r + S, slot);
-        }
+        if (r + S < rounds) issue(r + S, slot);
         if (OUT == OUT_DOTS) continue;
         // one thread per (output row, token): add the slices in order
         const int nout = min(rows_round, re - (rb + r * rows_round));

@@ -38,6 +38,25 @@ __device__ __forceinline__ void tma_bulk_load(void* dst, const void* src, uint32
                  ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
+// 16-byte copies global -> shared issued by this thread (LDGSTS), in commit groups.
+// Kernels launched with programmatic dependent launch use these for data they fetch
+// before griddepcontrol.wait, and each thread waits for its own groups with
+// cp_async_wait_upto before it blocks there: bulk copies a dependent grid issues
+// before the wait complete only once the previous grid has finished, and so do
+// completions that a thread parked in the wait would signal to an mbarrier.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Wait until at most n (0..2) of this thread's newest commit groups are pending.
+__device__ __forceinline__ void cp_async_wait_upto(int n) {
+    if (n <= 0)
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+    else if (n == 1)
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else
+        asm volatile("cp.async.wait_group 2;" ::: "memory");
+}
 // Wait for phase `parity` of the barrier, giving up after kWaitLimitCycles: a
 // non-blocking test first (the phase is usually complete by now), then the
 // hardware-suspending try_wait, so a waiting thread does not spin on the issue port.
