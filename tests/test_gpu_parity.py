@@ -349,6 +349,46 @@ def test_gemv_fused_quant_bit_exact(cuda, has_min, nk, m, mode):
         np.testing.assert_array_equal(bits(y.cpu().numpy()), bits(ref))
 
 
+@pytest.mark.parametrize("fq", [False, True])
+@pytest.mark.parametrize("has_min", [False, True])
+@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("n,k", [(6144, 2048), (2048, 6144), (2048, 4096), (512, 2048), (14000, 2048),
+                                 (3000, 1024), (600, 384), (1500, 2560), (20000, 2048)])
+def test_gemv_decode_shapes(cuda, n, k, m, mode, has_min, fq):
+    """The decode GEMV (one or two tokens into y) over each split of a row between
+    lanes (8, 16 or 32 lanes of one or two groups, idle lanes past the row's end),
+    one to four row passes per CTA, a zero activation row, and (20000, 2048), which
+    exceeds its shared-memory plan and takes the tensor-core GEMV.  Bit-exact with
+    the oracle (SWIGLU within 1e-3: expf) and with the dp4a GEMV, fused quant or not."""
+    q, s, _ = make_weight(n, k, 128, has_min, seed=n + k + m + mode)
+    x = make_x(m, k, seed=k + m)
+    if m == 2 and has_min:
+        x[1] = 0.0  # dx = 0, all codes 0
+    xq, xs = orc.quant(x, act=1)
+    n_out = n // 2 if mode == 2 else n
+    y0 = make_x(m, n_out, seed=6) if mode == 1 else None
+    ref = orc.gemv(q, s, k, 128, has_min, xq, xs, act=1, mode=mode, y=None if y0 is None else y0.copy())
+    w = dev_weight(q, s, n, k, 128, has_min, cuda)
+    base = lambda: None if y0 is None else to_dev(y0, cuda)  # noqa: E731
+    if fq:
+        y = ops.gemv_x(w, to_dev(x, cuda), mode=mode, y=base())
+    else:
+        y = ops.gemv(w, to_dev(xq, cuda), to_dev(xs, cuda), act=1, mode=mode, y=base())
+    ops.set_gemv_kernel(False)
+    try:
+        y_dp4a = ops.gemv(w, to_dev(xq, cuda), to_dev(xs, cuda), act=1, mode=mode, y=base())
+    finally:
+        ops.set_gemv_kernel(True)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(bits(y.cpu().numpy()), bits(y_dp4a.cpu().numpy()))
+    if mode == 2:
+        assert_rel_close(y.cpu().numpy(), ref, 1e-3)
+    else:
+        np.testing.assert_array_equal(bits(y.cpu().numpy()), bits(ref))
+    assert ops.device_error() == 0
+
+
 def test_gemv_fused_quant_rejects_group32(cuda):
     q, s, _ = make_weight(32, 256, 32, True, seed=1)
     w = dev_weight(q, s, 32, 256, 32, True, cuda)

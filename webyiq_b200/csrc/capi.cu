@@ -57,6 +57,8 @@ w4a8_status launch_quant(const float*, const float*, float, int, int, int, int8_
 w4a8_status launch_argmax(const float*, int, int, const uint32_t*, uint32_t*, cudaStream_t);
 
 w4a8_status launch_gemv_mma(const GemvParams& g, bool has_min, int mode, int out, cudaStream_t st);
+bool gemv_dec_covers(const GemvParams& g, int group, int act, int mode, int out);
+w4a8_status launch_gemv_dec(const GemvParams& g, bool has_min, int mode, cudaStream_t st);
 bool lmhead_stream_covers(const GemvParams& g, int group, int act);
 w4a8_status launch_lmhead_stream(const GemvParams& g, bool has_min, cudaStream_t st);
 w4a8_status device_error(unsigned int* code, cudaStream_t st);
@@ -77,6 +79,8 @@ w4a8_status launch_gemv(const GemvParams& p, int group, bool has_min, int act, i
     // per-token calls, the dp4a GEMV everything else.
     if (out == OUT_ARGMAX && g_use_mma && lmhead_stream_covers(p, group, act))
         return launch_lmhead_stream(p, has_min, st);
+    // One or two tokens into y whose rows fit the decode GEMV (gemv_dec.cu) go there.
+    if (g_use_mma && gemv_dec_covers(p, group, act, mode, out)) return launch_gemv_dec(p, has_min, mode, st);
     if (group == 128 && (act == W4A8_ACT_TOKEN || out == OUT_DOTS) && out != OUT_ARGMAX && g_use_mma)
         return launch_gemv_mma(p, has_min, mode, out, st);
     if (group == 32) return has_min ? launch_gemv_g32_m1(p, act, mode, out, st) : launch_gemv_g32_m0(p, act, mode, out, st);

@@ -1,0 +1,392 @@
+// Decode GEMV: one or two tokens, group-128 weights, per-token int8 activations
+// (or f32 activations quantized here), y = W x [+ y] or SWIGLU, for the
+// projection shapes of a decode step (a few MB of weights per call).
+//
+// Reference: gemv_q4q8.wgsl:36-131 (per-group math at :68, modes at :122-129) and
+// quant.wgsl for the fused per-token quantization.  Numerics: the exact per-token
+// path of w4a8.h (int64 sum over groups of fix16(s) * (I - 8 X) [+ fix16(min) * X],
+// then ((float)acc * 2^-24) * dx), bit-identical to the other GEMV kernels.
+//
+// Why this shape (B200 view).  A decode step is a chain of such calls, each waiting
+// for the previous one (griddepcontrol.wait), so what counts is the time from that
+// wait to the last store, not bandwidth: the weights (which do not depend on the
+// previous kernel) are fetched before the wait, and after it there is no CTA
+// barrier on the non-fused path.
+//  - One CTA per SM (two of consecutive calls fit on an SM, so the next call's
+//    copies run while this one computes) owns a balanced contiguous row range.
+//    Its rows are copied into shared memory with per-thread cp.async pieces, and
+//    each thread waits for its own pieces before the dependency wait: bulk copies
+//    issued by a dependent grid before griddepcontrol.wait complete only after the
+//    previous grid has finished.  The CTA's scale span travels the same way, and
+//    each lane decodes its groups' scales to (mantissa, shift) before the wait: a
+//    plain load still in flight at the wait would hold up the activation loads.
+//  - L lanes share a row (L = 8, 16 or 32) and each owns GPL whole 128-groups: the
+//    exact int32 group dot from its 4 x GPL 16-byte chunks (dp4a, low and high
+//    nibbles in separate accumulators), the group's int64 scale step, then log2(L)
+//    shuffles add the row; the row's first lane writes y.  Chunks are read in a
+//    per-lane rotated order so the 8 lanes of a shared-memory phase hit distinct
+//    bank groups (rows are stored unpadded).
+//  - The activations the lane meets stay in registers (32 x GPL per token), loaded
+//    straight from global memory after the wait (fused quant: quantized once per
+//    CTA into shared memory, then loaded from there).
+#include <cuda_fp16.h>
+
+#include "gemv.cuh"
+#include "launch.cuh"
+#include "tma.cuh"
+
+namespace w4a8 {
+
+int sm_count();  // capi.cu
+
+namespace {
+
+constexpr int kDecMaxPass = 4;                 // row passes per CTA (scale registers)
+constexpr size_t kDecSmemBudget = 100 * 1024;  // two CTAs per SM
+
+template <int MT, int GPL>
+struct DecThreads {
+    static constexpr int value = MT * GPL == 1 ? 384 : 256;  // two CTAs' registers fit an SM
+};
+
+struct DecParams {
+    const unsigned char* q;  // [rows][k/2]
+    const void* s;           // [rows][k/128] u16 f16 (symmetric) or u32 (scale | min << 16)
+    const int8_t* xq;        // [m][k]
+    const float* xs;         // [m] per-token dx
+    const float* xf32;       // [m][k] f32 activations to quantize here (FQ), else null
+    float* y;                // [m][y_stride]
+    int n_out, k, m, y_stride;
+    int L;         // lanes per row
+    int rows_max;  // rows of the largest CTA range
+    int sc_off;    // shared-memory offset of the scale spans (per half: sc_half bytes)
+    int sc_half;
+};
+
+__device__ __forceinline__ int pack_fix(uint32_t h) {
+    const Fix16 f = fix16(h);
+    return (f.mant << 8) | f.sh;
+}
+
+template <bool HAS_MIN, int MODE, int MT, int GPL, bool FQ>
+__global__ void __launch_bounds__(DecThreads<MT, GPL>::value, 2) gemv_dec_kernel(const DecParams p) {
+    constexpr bool SWI = MODE == W4A8_SWIGLU;
+    constexpr int NH = SWI ? 2 : 1;  // weight rows per output row (gate, up)
+    constexpr int kSteps = 4 * GPL;  // 16-byte chunks per lane per row
+    constexpr int T = DecThreads<MT, GPL>::value;
+    constexpr int NW = T / 32;
+    extern __shared__ __align__(128) unsigned char smem[];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = p.k, KG = K >> 7, KC = K >> 5, RB = K >> 1;
+    const int L = p.L, lsh = __ffs(L) - 1;
+    const int rb = static_cast<int>(static_cast<long long>(blockIdx.x) * p.n_out / gridDim.x);
+    const int re = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * p.n_out / gridDim.x);
+    const int nrow = re - rb;
+    const size_t hstride = static_cast<size_t>(p.rows_max) * RB;
+
+    pdl_launch_dependents();
+    // ---- before the dependency wait: this CTA's weight rows and the lane's scales ----
+    for (int i = warp; i < NH * nrow; i += NW) {
+        const int h = SWI ? (i >= nrow) : 0;
+        const int r = i - h * nrow;
+        const unsigned char* src = p.q + (static_cast<size_t>(rb + r) + static_cast<size_t>(h) * p.n_out) * RB;
+        unsigned char* dst = smem + h * hstride + static_cast<size_t>(r) * RB;
+        for (int c = lane; c < KC; c += 32) cp_async16(dst + c * 16, src + c * 16);
+    }
+    // the scale span of the CTA's rows (per half), widened to 16-byte boundaries
+    const int sbytes = HAS_MIN ? 4 : 2;
+    size_t sbase[NH];
+#pragma unroll
+    for (int h = 0; h < NH; ++h) {
+        const size_t b0 = (static_cast<size_t>(rb) + static_cast<size_t>(h) * p.n_out) * KG * sbytes;
+        const size_t b1 = b0 + static_cast<size_t>(nrow) * KG * sbytes;
+        const size_t a0 = b0 & ~static_cast<size_t>(15), a1 = (b1 + 15) & ~static_cast<size_t>(15);
+        sbase[h] = b0 - a0;
+        const unsigned char* src = static_cast<const unsigned char*>(p.s) + a0;
+        unsigned char* dst = smem + p.sc_off + h * p.sc_half;
+        for (int i = tid; i < static_cast<int>((a1 - a0) >> 4); i += T) cp_async16(dst + i * 16, src + i * 16);
+    }
+    cp_async_commit();
+
+    const int j = lane & (L - 1);  // the lane's span of a row: groups [j*GPL, j*GPL + GPL)
+    const int ph = lane & 7;       // position in its 16-byte shared-memory phase
+    // rotation: step c reads chunk (c%4 + rc) % 4 of group j*GPL + (c/4 + rg) % GPL
+    const int rg = (GPL % 2 == 0) ? (ph >> 2) & 1 : 0;
+    const int rc = (GPL % 2 == 0) ? (ph & 3) : ((ph >> 1) & 3);
+    int gidx[GPL];
+    bool gin[GPL];
+#pragma unroll
+    for (int g = 0; g < GPL; ++g) {
+        gidx[g] = j * GPL + (g + rg) % GPL;
+        gin[g] = gidx[g] < KG;
+    }
+    int coff[kSteps];  // byte offset of step c's chunk in the packed row
+#pragma unroll
+    for (int c = 0; c < kSteps; ++c) coff[c] = (gidx[c / 4] * 4 + (c % 4 + rc) % 4) * 16;
+
+    const int rpw = 32 >> lsh;  // rows a warp takes per pass
+    const int npass = (nrow + NW * rpw - 1) / (NW * rpw);
+    cp_async_wait_upto(0);  // this thread's pieces have landed
+    __syncthreads();        // and everyone's
+    // decoded scales (and mins) of this lane's groups, [pass][h][g]
+    int sfx[kDecMaxPass][NH][GPL], mfx[kDecMaxPass][NH][GPL];
+#pragma unroll
+    for (int ps = 0; ps < kDecMaxPass; ++ps) {
+        const int rl = (ps * NW + warp) * rpw + (lane >> lsh);
+#pragma unroll
+        for (int h = 0; h < NH; ++h)
+#pragma unroll
+            for (int g = 0; g < GPL; ++g) {
+                sfx[ps][h][g] = mfx[ps][h][g] = 0;
+                if (ps < npass && rl < nrow && gin[g]) {
+                    const unsigned char* sp =
+                        smem + p.sc_off + h * p.sc_half + sbase[h] + (static_cast<size_t>(rl) * KG + gidx[g]) * sbytes;
+                    if (HAS_MIN) {
+                        const uint32_t w = *reinterpret_cast<const uint32_t*>(sp);
+                        sfx[ps][h][g] = pack_fix(w & 0xffffu);
+                        mfx[ps][h][g] = pack_fix(w >> 16);
+                    } else {
+                        sfx[ps][h][g] = pack_fix(*reinterpret_cast<const unsigned short*>(sp));
+                    }
+                }
+            }
+    }
+    pdl_wait();  // activations (and y for ADD) come from the previous kernel
+
+    // ---- activations of the lane's chunks, their group sums, dx ----
+    uint4 xa[MT][kSteps], xb[MT][kSteps];
+    int Xg[MT][GPL];
+    float dx[MT];
+    if (FQ) {
+        // per-token quantization (quant.wgsl with one scale per token), exactly as
+        // w4a8_quant computes it: amax, dx = amax / 127, inv = 1 / dx (0 for a zero
+        // row), rint(x * inv); the CTA writes the int8 row into shared memory once.
+        __shared__ unsigned int s_amax[2];
+        int8_t* xsm = reinterpret_cast<int8_t*>(smem + p.sc_off + NH * p.sc_half);
+        if (tid < MT) s_amax[tid] = 0u;
+        __syncthreads();
+        for (int t = 0; t < p.m; ++t) {
+            float a = 0.0f;
+            const float4* src = reinterpret_cast<const float4*>(p.xf32 + static_cast<size_t>(t) * K);
+            for (int i = tid; i < K / 4; i += T) {
+                const float4 v = __ldg(src + i);
+                a = fmaxf(fmaxf(a, fabsf(v.x)), fmaxf(fmaxf(fabsf(v.y), fabsf(v.z)), fabsf(v.w)));
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(kFull, a, off));
+            if (lane == 0) atomicMax(&s_amax[t], __float_as_uint(a));
+        }
+        __syncthreads();
+        for (int t = 0; t < p.m; ++t) {
+            const float a = __uint_as_float(s_amax[t]);
+            const float inv = a > 0.0f ? __fdiv_rn(1.0f, __fdiv_rn(a, 127.0f)) : 0.0f;
+            const float4* src = reinterpret_cast<const float4*>(p.xf32 + static_cast<size_t>(t) * K);
+            uint32_t* dst = reinterpret_cast<uint32_t*>(xsm + static_cast<size_t>(t) * K);
+            for (int i = tid; i < K / 4; i += T) {
+                const float4 v = __ldg(src + i);
+                const int q0 = static_cast<int>(rintf(__fmul_rn(v.x, inv)));
+                const int q1 = static_cast<int>(rintf(__fmul_rn(v.y, inv)));
+                const int q2 = static_cast<int>(rintf(__fmul_rn(v.z, inv)));
+                const int q3 = static_cast<int>(rintf(__fmul_rn(v.w, inv)));
+                dst[i] = (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
+                         ((static_cast<uint32_t>(q2) & 0xffu) << 16) | ((static_cast<uint32_t>(q3) & 0xffu) << 24);
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+            dx[t] = t < p.m ? __fdiv_rn(__uint_as_float(s_amax[t]), 127.0f) : 0.0f;
+#pragma unroll
+            for (int g = 0; g < GPL; ++g) Xg[t][g] = 0;
+#pragma unroll
+            for (int c = 0; c < kSteps; ++c) {
+                xa[t][c] = xb[t][c] = make_uint4(0, 0, 0, 0);
+                if (t < p.m && gin[c / 4]) {
+                    const uint4* xp = reinterpret_cast<const uint4*>(xsm + static_cast<size_t>(t) * K + coff[c] * 2);
+                    xa[t][c] = xp[0];
+                    xb[t][c] = xp[1];
+                }
+                Xg[t][c / 4] += chunk_sum(xa[t][c], xb[t][c]);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+            dx[t] = t < p.m ? __ldg(p.xs + t) : 0.0f;
+#pragma unroll
+            for (int g = 0; g < GPL; ++g) Xg[t][g] = 0;
+#pragma unroll
+            for (int c = 0; c < kSteps; ++c) {
+                xa[t][c] = xb[t][c] = make_uint4(0, 0, 0, 0);
+                if (t < p.m && gin[c / 4]) {
+                    const uint4* xp = reinterpret_cast<const uint4*>(p.xq + static_cast<size_t>(t) * K + coff[c] * 2);
+                    xa[t][c] = __ldg(xp);
+                    xb[t][c] = __ldg(xp + 1);
+                }
+                Xg[t][c / 4] += chunk_sum(xa[t][c], xb[t][c]);
+            }
+        }
+    }
+
+    // ---- row passes ----
+#pragma unroll
+    for (int ps = 0; ps < kDecMaxPass; ++ps) {
+        if (ps >= npass) break;
+        const int rl = (ps * NW + warp) * rpw + (lane >> lsh);
+        const bool rin = rl < nrow;
+        long long acc[NH][MT];
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+            const unsigned char* row = smem + h * hstride + static_cast<size_t>(rin ? rl : 0) * RB;
+            uint4 w[kSteps];
+#pragma unroll
+            for (int c = 0; c < kSteps; ++c)
+                w[c] = (rin && gin[c / 4]) ? *reinterpret_cast<const uint4*>(row + coff[c]) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int t = 0; t < MT; ++t) {
+                acc[h][t] = 0;
+#pragma unroll
+                for (int g = 0; g < GPL; ++g) {
+                    const uint32_t ml = 0x0F0F0F0Fu, mh = 0xF0F0F0F0u;
+                    int lo = 0, hi = 0;
+#pragma unroll
+                    for (int c = 4 * g; c < 4 * g + 4; ++c) {
+                        lo = dp4a_us(w[c].x & ml, xa[t][c].x, lo);
+                        hi = dp4a_us(w[c].x & mh, xa[t][c].y, hi);
+                        lo = dp4a_us(w[c].y & ml, xa[t][c].z, lo);
+                        hi = dp4a_us(w[c].y & mh, xa[t][c].w, hi);
+                        lo = dp4a_us(w[c].z & ml, xb[t][c].x, lo);
+                        hi = dp4a_us(w[c].z & mh, xb[t][c].y, hi);
+                        lo = dp4a_us(w[c].w & ml, xb[t][c].z, lo);
+                        hi = dp4a_us(w[c].w & mh, xb[t][c].w, hi);
+                    }
+                    const int I = lo + (hi >> 4);  // hi is an exact multiple of 16
+                    const int sf = sfx[ps][h][g];
+                    if (HAS_MIN) {
+                        const int mf = mfx[ps][h][g];
+                        acc[h][t] += shl64((sf >> 8) * I, sf & 0xff) + shl64((mf >> 8) * Xg[t][g], mf & 0xff);
+                    } else {
+                        acc[h][t] += shl64((sf >> 8) * (I - 8 * Xg[t][g]), sf & 0xff);
+                    }
+                }
+            }
+        }
+        for (int off = 1; off < L; off <<= 1)
+#pragma unroll
+            for (int h = 0; h < NH; ++h)
+#pragma unroll
+                for (int t = 0; t < MT; ++t) acc[h][t] += shfl_xor_i64(acc[h][t], off);
+        if (j == 0 && rin) {
+#pragma unroll
+            for (int t = 0; t < MT; ++t) {
+                if (t >= p.m) continue;
+                float v = fix_to_float(acc[0][t], dx[t]);
+                float* yp = p.y + static_cast<size_t>(t) * p.y_stride + rb + rl;
+                if (SWI)
+                    *yp = silu_mul(v, fix_to_float(acc[NH - 1][t], dx[t]));
+                else if (MODE == W4A8_ADD)
+                    *yp = __fadd_rn(*yp, v);
+                else
+                    *yp = v;
+            }
+        }
+    }
+}
+
+// Lanes per row and groups per lane: the smallest L in {8, 16, 32} covering the row
+// with GPL * MT <= 2 groups' activations in registers; L = 0 when none does.
+struct DecShape {
+    int L, gpl;
+};
+DecShape dec_shape(int kg, int m) {
+    for (int gpl = 1; gpl <= (m == 1 ? 2 : 1); ++gpl)
+        for (int L = 8; L <= 32; L <<= 1)
+            if (kg <= L * gpl) return {L, gpl};
+    return {0, 0};
+}
+
+struct DecPlan {
+    DecShape sh;
+    int ctas, rows_max, threads;
+    int sc_off, sc_half;
+    size_t smem;
+};
+
+bool dec_plan(const GemvParams& g, bool has_min, int mode, DecPlan& pl) {
+    if (g.m < 1 || g.m > 2 || g.k % 128 != 0 || g.n_out < 1) return false;
+    pl.sh = dec_shape(g.k / 128, g.m);
+    if (pl.sh.L == 0) return false;
+    pl.threads = g.m * pl.sh.gpl == 1 ? 384 : 256;
+    const int sms = sm_count();
+    pl.ctas = g.n_out < sms ? g.n_out : sms;
+    pl.rows_max = (g.n_out + pl.ctas - 1) / pl.ctas;
+    const int nh = mode == W4A8_SWIGLU ? 2 : 1;
+    const int sbytes = has_min ? 4 : 2;
+    pl.sc_off = nh * pl.rows_max * (g.k / 2);
+    pl.sc_half = ((pl.rows_max * (g.k / 128) * sbytes + 15) & ~15) + 16;  // + the widening to 16 bytes
+    pl.smem = static_cast<size_t>(pl.sc_off) + static_cast<size_t>(nh) * pl.sc_half +
+              (g.xf32 ? static_cast<size_t>(g.m) * g.k : 0);
+    const int rows_per_pass = (pl.threads / 32) * (32 / pl.sh.L);
+    const int npass = (pl.rows_max + rows_per_pass - 1) / rows_per_pass;
+    return pl.smem <= kDecSmemBudget && npass <= kDecMaxPass;
+}
+
+template <bool HAS_MIN, int MODE, int MT, int GPL, bool FQ>
+w4a8_status dec_inst(const DecParams& p, const DecPlan& pl, cudaStream_t st) {
+    static size_t configured = 0;  // set on first use: static shared memory counts against the default 48 KB too
+    auto kernel = gemv_dec_kernel<HAS_MIN, MODE, MT, GPL, FQ>;
+    if (pl.smem > configured) {
+        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pl.smem));
+        if (e != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8 gemv (decode): smem attribute: %s", cudaGetErrorString(e));
+        configured = pl.smem;
+    }
+    return launch_pdl("w4a8 gemv (decode)", kernel, dim3(pl.ctas), dim3(DecThreads<MT, GPL>::value), pl.smem, st, p);
+}
+
+template <bool HAS_MIN, int MODE, bool FQ>
+w4a8_status dec_shape_dispatch(const DecParams& p, const DecPlan& pl, cudaStream_t st) {
+    if (p.m == 1) return pl.sh.gpl == 1 ? dec_inst<HAS_MIN, MODE, 1, 1, FQ>(p, pl, st) : dec_inst<HAS_MIN, MODE, 1, 2, FQ>(p, pl, st);
+    return dec_inst<HAS_MIN, MODE, 2, 1, FQ>(p, pl, st);
+}
+
+template <bool HAS_MIN, bool FQ>
+w4a8_status dec_mode_dispatch(const DecParams& p, const DecPlan& pl, int mode, cudaStream_t st) {
+    if (mode == W4A8_STORE) return dec_shape_dispatch<HAS_MIN, W4A8_STORE, FQ>(p, pl, st);
+    if (mode == W4A8_ADD) return dec_shape_dispatch<HAS_MIN, W4A8_ADD, FQ>(p, pl, st);
+    return dec_shape_dispatch<HAS_MIN, W4A8_SWIGLU, FQ>(p, pl, st);
+}
+
+}  // namespace
+
+// Whether the decode GEMV covers this call: group 128, per-token activations, the
+// y output, one or two tokens, and a per-CTA row range that fits shared memory.
+bool gemv_dec_covers(const GemvParams& g, int group, int act, int mode, int out) {
+    if (group != 128 || act != W4A8_ACT_TOKEN || out != OUT_Y) return false;
+    DecPlan pl;
+    return dec_plan(g, true, mode, pl);  // the larger (u32) scale span
+}
+
+w4a8_status launch_gemv_dec(const GemvParams& g, bool has_min, int mode, cudaStream_t st) {
+    DecPlan pl;
+    if (!dec_plan(g, has_min, mode, pl)) return set_error(W4A8_EINVAL, "w4a8 gemv (decode): call not covered");
+    DecParams p{};
+    p.q = reinterpret_cast<const unsigned char*>(g.q);
+    p.s = g.s;
+    p.xq = g.xq;
+    p.xs = g.xs;
+    p.xf32 = g.xf32;
+    p.y = g.y;
+    p.n_out = g.n_out;
+    p.k = g.k;
+    p.m = g.m;
+    p.y_stride = g.y_stride;
+    p.L = pl.sh.L;
+    p.rows_max = pl.rows_max;
+    p.sc_off = pl.sc_off;
+    p.sc_half = pl.sc_half;
+    if (g.xf32) return has_min ? dec_mode_dispatch<true, true>(p, pl, mode, st) : dec_mode_dispatch<false, true>(p, pl, mode, st);
+    return has_min ? dec_mode_dispatch<true, false>(p, pl, mode, st) : dec_mode_dispatch<false, false>(p, pl, mode, st);
+}
+
+}  // namespace w4a8

@@ -12,7 +12,7 @@ namespace {
 // RT tiles of 16 rows (8 output rows for SWIGLU); RT x KS warps, KS = ceil(KG/4).
 template <bool HAS_MIN, int MODE, int OUT, int MT, bool FQ>
 w4a8_status launch_mt(MmaParams p, cudaStream_t st) {
-    static size_t configured = 48 * 1024;
+    static size_t configured = 0;  // set on first use: static shared memory counts against the default 48 KB too
     auto kernel = gemv_mma_kernel<HAS_MIN, MODE, OUT, MT, FQ>;
     const int kg = p.k / 128;
     p.ks = (kg + kMmaGPS - 1) / kMmaGPS;
