@@ -197,6 +197,8 @@ w4a8_status w4a8_gemv_x(const w4a8_weight* w, const float* x, int32_t m, int32_t
     p.y_stride = p.n_out;
     p.k = w->k;
     p.m = m;
+    if (g_use_mma && gemv_dec_covers(p, 128, W4A8_ACT_TOKEN, mode, OUT_Y))
+        return launch_gemv_dec(p, w->has_min != 0, mode, static_cast<cudaStream_t>(stream));
     return launch_gemv_mma(p, w->has_min != 0, mode, OUT_Y, static_cast<cudaStream_t>(stream));
 }
 

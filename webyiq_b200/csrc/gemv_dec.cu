@@ -42,6 +42,7 @@ int sm_count();  // capi.cu
 namespace {
 
 constexpr int kDecMaxPass = 4;                 // row passes per CTA (scale registers)
+constexpr int kDecVPT = 8;                     // fused quant: float4s of x per thread (per token)
 constexpr size_t kDecSmemBudget = 100 * 1024;  // two CTAs per SM
 
 template <int MT, int GPL>
@@ -127,6 +128,17 @@ __global__ void __launch_bounds__(DecThreads<MT, GPL>::value, 2) gemv_dec_kernel
 
     const int rpw = 32 >> lsh;  // rows a warp takes per pass
     const int npass = (nrow + NW * rpw - 1) / (NW * rpw);
+    // The activations towards L2: a prefetch returns no data, so a line the previous
+    // kernel still writes is read afresh after the wait; a line it does not write
+    // (an input copied in long before) then comes from L2 instead of DRAM.
+    {
+        const char* xb0 = FQ ? reinterpret_cast<const char*>(p.xf32) : reinterpret_cast<const char*>(p.xq);
+        const int lines = (p.m * K * (FQ ? 4 : 1) + 127) >> 7;
+        for (int i = tid; i < lines; i += T) asm volatile("prefetch.global.L2 [%0];" ::"l"(xb0 + (static_cast<size_t>(i) << 7)));
+        if (!FQ && tid == 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.xs));
+    }
+    __shared__ unsigned int s_amax[2];  // fused quant: per-token absmax as float bits
+    if (FQ && tid < 2) s_amax[tid] = 0u;
     cp_async_wait_upto(0);  // this thread's pieces have landed
     __syncthreads();        // and everyone's
     // decoded scales (and mins) of this lane's groups, [pass][h][g]
@@ -161,34 +173,42 @@ __global__ void __launch_bounds__(DecThreads<MT, GPL>::value, 2) gemv_dec_kernel
     if (FQ) {
         // per-token quantization (quant.wgsl with one scale per token), exactly as
         // w4a8_quant computes it: amax, dx = amax / 127, inv = 1 / dx (0 for a zero
-        // row), rint(x * inv); the CTA writes the int8 row into shared memory once.
-        __shared__ unsigned int s_amax[2];
+        // row), rint(x * inv).  One pass over x: each thread keeps its float4s in
+        // registers across the amax exchange, then writes their int8 codes into
+        // shared memory, where the lanes read the chunks they meet.
         int8_t* xsm = reinterpret_cast<int8_t*>(smem + p.sc_off + NH * p.sc_half);
-        if (tid < MT) s_amax[tid] = 0u;
-        __syncthreads();
-        for (int t = 0; t < p.m; ++t) {
+        constexpr int VPT = MT == 1 ? kDecVPT : kDecVPT / 2;
+        float4 v[MT][VPT];
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
             float a = 0.0f;
             const float4* src = reinterpret_cast<const float4*>(p.xf32 + static_cast<size_t>(t) * K);
-            for (int i = tid; i < K / 4; i += T) {
-                const float4 v = __ldg(src + i);
-                a = fmaxf(fmaxf(a, fabsf(v.x)), fmaxf(fmaxf(fabsf(v.y), fabsf(v.z)), fabsf(v.w)));
+#pragma unroll
+            for (int u = 0; u < VPT; ++u) {
+                const int i = tid + u * T;
+                v[t][u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (t < p.m && i < K / 4) v[t][u] = __ldg(src + i);
+                a = fmaxf(fmaxf(a, fabsf(v[t][u].x)), fmaxf(fmaxf(fabsf(v[t][u].y), fabsf(v[t][u].z)), fabsf(v[t][u].w)));
             }
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(kFull, a, off));
-            if (lane == 0) atomicMax(&s_amax[t], __float_as_uint(a));
+            if (lane == 0 && t < p.m) atomicMax(&s_amax[t], __float_as_uint(a));
         }
         __syncthreads();
-        for (int t = 0; t < p.m; ++t) {
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+            if (t >= p.m) continue;
             const float a = __uint_as_float(s_amax[t]);
             const float inv = a > 0.0f ? __fdiv_rn(1.0f, __fdiv_rn(a, 127.0f)) : 0.0f;
-            const float4* src = reinterpret_cast<const float4*>(p.xf32 + static_cast<size_t>(t) * K);
             uint32_t* dst = reinterpret_cast<uint32_t*>(xsm + static_cast<size_t>(t) * K);
-            for (int i = tid; i < K / 4; i += T) {
-                const float4 v = __ldg(src + i);
-                const int q0 = static_cast<int>(rintf(__fmul_rn(v.x, inv)));
-                const int q1 = static_cast<int>(rintf(__fmul_rn(v.y, inv)));
-                const int q2 = static_cast<int>(rintf(__fmul_rn(v.z, inv)));
-                const int q3 = static_cast<int>(rintf(__fmul_rn(v.w, inv)));
+#pragma unroll
+            for (int u = 0; u < VPT; ++u) {
+                const int i = tid + u * T;
+                if (i >= K / 4) continue;
+                const int q0 = static_cast<int>(rintf(__fmul_rn(v[t][u].x, inv)));
+                const int q1 = static_cast<int>(rintf(__fmul_rn(v[t][u].y, inv)));
+                const int q2 = static_cast<int>(rintf(__fmul_rn(v[t][u].z, inv)));
+                const int q3 = static_cast<int>(rintf(__fmul_rn(v[t][u].w, inv)));
                 dst[i] = (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
                          ((static_cast<uint32_t>(q2) & 0xffu) << 16) | ((static_cast<uint32_t>(q3) & 0xffu) << 24);
             }
@@ -329,7 +349,8 @@ bool dec_plan(const GemvParams& g, bool has_min, int mode, DecPlan& pl) {
               (g.xf32 ? static_cast<size_t>(g.m) * g.k : 0);
     const int rows_per_pass = (pl.threads / 32) * (32 / pl.sh.L);
     const int npass = (pl.rows_max + rows_per_pass - 1) / rows_per_pass;
-    return pl.smem <= kDecSmemBudget && npass <= kDecMaxPass;
+    const bool vpt_ok = !g.xf32 || (g.k / 4 + pl.threads - 1) / pl.threads <= (g.m == 1 ? kDecVPT : kDecVPT / 2);
+    return pl.smem <= kDecSmemBudget && npass <= kDecMaxPass && vpt_ok;
 }
 
 template <bool HAS_MIN, int MODE, int MT, int GPL, bool FQ>
