@@ -10,8 +10,8 @@
 // Why this shape (B200 view).  A decode step is a chain of such calls, each waiting
 // for the previous one (griddepcontrol.wait), so what counts is the time from that
 // wait to the last store, not bandwidth: the weights (which do not depend on the
-// previous kernel) are fetched before the wait, and after it there is no CTA
-// barrier on the non-fused path.
+// previous kernel) are fetched before the wait, and after it the CTA meets no
+// barrier (two with fused quant).
 //  - One CTA per SM (two of consecutive calls fit on an SM, so the next call's
 //    copies run while this one computes) owns a balanced contiguous row range.
 //    Its rows are copied into shared memory with per-thread cp.async pieces, and
@@ -26,9 +26,11 @@
 //    shuffles add the row; the row's first lane writes y.  Chunks are read in a
 //    per-lane rotated order so the 8 lanes of a shared-memory phase hit distinct
 //    bank groups (rows are stored unpadded).
-//  - The activations the lane meets stay in registers (32 x GPL per token), loaded
-//    straight from global memory after the wait (fused quant: quantized once per
-//    CTA into shared memory, then loaded from there).
+//  - The activations the lane meets stay in registers (32 x GPL per token): int8
+//    activations come straight from global memory after the wait, with no CTA
+//    barrier; fused quant stages the row once per CTA in shared memory (one pass
+//    over the f32 row, the absmax exchanged by a shared atomicMax, group sums from
+//    warp shuffles) and the lanes read their chunks from there.
 #include <cuda_fp16.h>
 
 #include "gemv.cuh"
@@ -138,6 +140,7 @@ __global__ void __launch_bounds__(DecThreads<MT, GPL>::value, 2) gemv_dec_kernel
         if (!FQ && tid == 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.xs));
     }
     __shared__ unsigned int s_amax[2];  // fused quant: per-token absmax as float bits
+    __shared__ float s_dx[2];
     if (FQ && tid < 2) s_amax[tid] = 0u;
     cp_async_wait_upto(0);  // this thread's pieces have landed
     __syncthreads();        // and everyone's
@@ -166,17 +169,23 @@ __global__ void __launch_bounds__(DecThreads<MT, GPL>::value, 2) gemv_dec_kernel
     }
     pdl_wait();  // activations (and y for ADD) come from the previous kernel
 
-    // ---- activations of the lane's chunks, their group sums, dx ----
-    uint4 xa[MT][kSteps], xb[MT][kSteps];
-    int Xg[MT][GPL];
+    // ---- activations ----
+    // Fused quant stages the quantized rows once per CTA in shared memory, per token:
+    // the first 16 bytes of every 32-byte chunk, then the second 16 bytes (so the
+    // lanes' rotated chunk reads are conflict-free), and the group sums X[KG].
+    const int xrow = K + ((KG * 4 + 15) & ~15);  // bytes per token (16-byte multiple)
+    unsigned char* xsm = smem + p.sc_off + NH * p.sc_half;
+    auto xhalf = [&](int t, int h, int ci) -> unsigned char* {  // 16-byte half h of chunk ci
+        return xsm + static_cast<size_t>(t) * xrow + h * (K / 2) + ci * 16;
+    };
+    auto xgrp = [&](int t) -> int* { return reinterpret_cast<int*>(xsm + static_cast<size_t>(t) * xrow + K); };
     float dx[MT];
     if (FQ) {
         // per-token quantization (quant.wgsl with one scale per token), exactly as
         // w4a8_quant computes it: amax, dx = amax / 127, inv = 1 / dx (0 for a zero
         // row), rint(x * inv).  One pass over x: each thread keeps its float4s in
-        // registers across the amax exchange, then writes their int8 codes into
-        // shared memory, where the lanes read the chunks they meet.
-        int8_t* xsm = reinterpret_cast<int8_t*>(smem + p.sc_off + NH * p.sc_half);
+        // registers across the amax exchange.  A warp's 32 neighbouring float4s are
+        // one 128-group, so the group sums come from warp shuffles.
         constexpr int VPT = MT == 1 ? kDecVPT : kDecVPT / 2;
         float4 v[MT][VPT];
 #pragma unroll
@@ -200,37 +209,50 @@ __global__ void __launch_bounds__(DecThreads<MT, GPL>::value, 2) gemv_dec_kernel
             if (t >= p.m) continue;
             const float a = __uint_as_float(s_amax[t]);
             const float inv = a > 0.0f ? __fdiv_rn(1.0f, __fdiv_rn(a, 127.0f)) : 0.0f;
-            uint32_t* dst = reinterpret_cast<uint32_t*>(xsm + static_cast<size_t>(t) * K);
 #pragma unroll
             for (int u = 0; u < VPT; ++u) {
-                const int i = tid + u * T;
-                if (i >= K / 4) continue;
+                const int i = tid + u * T;  // float4 index: elements 4i..4i+3
+                if (u * T >= K / 4) break;   // warp-uniform (K / 4 is a multiple of 32)
                 const int q0 = static_cast<int>(rintf(__fmul_rn(v[t][u].x, inv)));
                 const int q1 = static_cast<int>(rintf(__fmul_rn(v[t][u].y, inv)));
                 const int q2 = static_cast<int>(rintf(__fmul_rn(v[t][u].z, inv)));
                 const int q3 = static_cast<int>(rintf(__fmul_rn(v[t][u].w, inv)));
-                dst[i] = (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
-                         ((static_cast<uint32_t>(q2) & 0xffu) << 16) | ((static_cast<uint32_t>(q3) & 0xffu) << 24);
+                int X = 0;
+                if (i < K / 4) {
+                    *reinterpret_cast<uint32_t*>(xhalf(t, (i >> 2) & 1, i >> 3) + (i & 3) * 4) =
+                        (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
+                        ((static_cast<uint32_t>(q2) & 0xffu) << 16) | ((static_cast<uint32_t>(q3) & 0xffu) << 24);
+                    X = q0 + q1 + q2 + q3;
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) X += __shfl_xor_sync(kFull, X, off);
+                if (lane == 0 && i < K / 4) xgrp(t)[i >> 5] = X;
             }
+            if (tid == 0) s_dx[t] = __fdiv_rn(a, 127.0f);
         }
+    }
+    uint4 xa[MT][kSteps], xb[MT][kSteps];
+    int Xg[MT][GPL];
+    if (FQ) {
         __syncthreads();
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
-            dx[t] = t < p.m ? __fdiv_rn(__uint_as_float(s_amax[t]), 127.0f) : 0.0f;
+            dx[t] = t < p.m ? s_dx[t] : 0.0f;
 #pragma unroll
-            for (int g = 0; g < GPL; ++g) Xg[t][g] = 0;
+            for (int g = 0; g < GPL; ++g) Xg[t][g] = (t < p.m && gin[g]) ? xgrp(t)[gidx[g]] : 0;
 #pragma unroll
             for (int c = 0; c < kSteps; ++c) {
                 xa[t][c] = xb[t][c] = make_uint4(0, 0, 0, 0);
                 if (t < p.m && gin[c / 4]) {
-                    const uint4* xp = reinterpret_cast<const uint4*>(xsm + static_cast<size_t>(t) * K + coff[c] * 2);
-                    xa[t][c] = xp[0];
-                    xb[t][c] = xp[1];
+                    const int ci = coff[c] >> 4;  // chunk index in the row
+                    xa[t][c] = *reinterpret_cast<const uint4*>(xhalf(t, 0, ci));
+                    xb[t][c] = *reinterpret_cast<const uint4*>(xhalf(t, 1, ci));
                 }
-                Xg[t][c / 4] += chunk_sum(xa[t][c], xb[t][c]);
             }
         }
     } else {
+        // int8 activations: each lane loads the chunks it meets straight from global
+        // memory (no CTA barrier) and sums its groups itself
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
             dx[t] = t < p.m ? __ldg(p.xs + t) : 0.0f;
@@ -346,7 +368,7 @@ bool dec_plan(const GemvParams& g, bool has_min, int mode, DecPlan& pl) {
     pl.sc_off = nh * pl.rows_max * (g.k / 2);
     pl.sc_half = ((pl.rows_max * (g.k / 128) * sbytes + 15) & ~15) + 16;  // + the widening to 16 bytes
     pl.smem = static_cast<size_t>(pl.sc_off) + static_cast<size_t>(nh) * pl.sc_half +
-              (g.xf32 ? static_cast<size_t>(g.m) * g.k : 0);
+              (g.xf32 ? static_cast<size_t>(g.m) * (g.k + (((g.k / 128) * 4 + 15) & ~15)) : 0);  // fused quant staging
     const int rows_per_pass = (pl.threads / 32) * (32 / pl.sh.L);
     const int npass = (pl.rows_max + rows_per_pass - 1) / rows_per_pass;
     const bool vpt_ok = !g.xf32 || (g.k / 4 + pl.threads - 1) / pl.threads <= (g.m == 1 ? kDecVPT : kDecVPT / 2);
