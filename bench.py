@@ -576,7 +576,7 @@ def main():
                        "parallelism": f"replicas x{world}", "launch": "cuda graph, PDL between GEMVs"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "peak_kind": peak_kind, "traffic": traffic,
-                         "kernel": "gemv_mma_kernel (group-128 per-token GEMV)",
+                         "kernel": "gemv_dec_kernel (decode GEMV, group-128 per-token)",
                          "algorithmic_bytes_per_launch": round(sb / Sweep.launches_per_step),
                          "launch_us": round(ms * 1e3 / Sweep.launches_per_step, 3)},
             "e2e": {"value": round(e2e, 1), "unit": "GB/s", "ms_per_step": round(ms_e2e, 4),
