@@ -37,10 +37,11 @@
 //    Four TMEM buffers of 128 columns (all 512) let the tensor core run four
 //    groups ahead of the epilogue.
 //
-// Warp roles per CTA (12 warps, 168 registers each): 0 activation TMA, 1 MMA
-// issue (cluster rank 0 only; a tcgen05.mma blocks its thread for about its own
-// duration) and TMEM allocation, 2-3 int4 -> int8 expansion, 4-11 epilogue (two
-// halves of 64 columns; warp % 4 is the TMEM lane quadrant a warp may read).
+// Warp roles per CTA (10 warps, 200 registers each): 0 weight and activation TMA,
+// 1 MMA issue (cluster rank 0 only; a tcgen05.mma blocks its thread for about its
+// own duration) and TMEM allocation, 2-9 epilogue: int4 -> int8 expansion kLead
+// groups ahead and the scale step (two halves of 64 columns; warp % 4 is the TMEM
+// lane quadrant a warp may access).
 // Barriers that the MMA waits on (int8 tiles written, accumulators released)
 // live in rank 0 and both CTAs arrive on them; the MMA's completions arrive on
 // both CTAs' barriers (one tcgen05.commit per CTA).  Every wait is bounded; a wait
@@ -75,8 +76,8 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA = kDBufs * kTok;  // first column of the weight tiles
 static_assert(kTmemA + kABufs * 32 <= kTmemCols, "TMEM plan exceeds 512 columns");
 static_assert(kLead < kABufs && kLead < kDBufs + 1, "expansion lead exceeds the buffers");
-constexpr int kEpiWarp0 = 4, kEpiWarps = 8;
-constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 384: 168 registers per thread
+constexpr int kEpiWarp0 = 2, kEpiWarps = 8;
+constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 320: 200 registers per thread
 constexpr uint32_t kBias = 0x4B400000u;                  // bits of 1.5 * 2^23
 constexpr float kBiasF = 12582912.0f;
 
@@ -252,9 +253,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + bar_offset(SWI));  // stage copies landed (local)
     uint64_t* empty = full + kStages;     // MMA done with a stage (both)
     uint64_t* aready = empty + kStages;   // int8 weight tile written to TMEM (rank 0; both CTAs arrive)
-    uint64_t* aempty = aready + kABufs;   // MMA done with an int8 weight tile (both)
-    uint64_t* accf = aempty + kABufs;     // group accumulator complete (both)
-    uint64_t* acce = accf + kDBufs;       // accumulator read and re-biased (rank 0; both arrive)
+    // The MMAs of group j complete (both CTAs, one ring of kABufs): accumulator j
+    // may be read, and weight tile j % kABufs may be rewritten for group j + kABufs.
+    uint64_t* gdone = aready + kABufs;
+    uint64_t* acce = gdone + kABufs;      // accumulator read and re-biased (rank 0; both arrive)
     uint64_t* done = acce + kDBufs;       // all MMAs complete (rank 0)
     uint64_t* xbar = done + 1;            // SWIGLU exchange, one per column half (local)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 2);
@@ -269,12 +271,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < kABufs; ++a) {
             mbar_init(aready + a, 2 * kEpiWarps);  // one arrival per epilogue warp of each CTA
-            mbar_init(aempty + a, 1);
+            mbar_init(gdone + a, 1);
         }
-        for (int b = 0; b < kDBufs; ++b) {
-            mbar_init(accf + b, 1);
-            mbar_init(acce + b, 2 * kEpiWarps);
-        }
+        for (int b = 0; b < kDBufs; ++b) mbar_init(acce + b, 2 * kEpiWarps);
         mbar_init(done, 1);
         mbar_init(xbar, 128);
         mbar_init(xbar + 1, 128);
@@ -354,8 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t at = tmem + kTmemA + a * 32;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) mma_i8_pair_ts(d, at + kk * 8, sw128_desc(x_addr + 32 * kk), kIdesc);
-                    tc_commit_pair(aempty + a);
-                    tc_commit_pair(accf + b);
+                    tc_commit_pair(gdone + a);
                     if (g % kSG == kSG - 1 || g == kg - 1) {
                         tc_commit_pair(empty + s);
                         ++js;
@@ -392,10 +390,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t jd = 0, sde = 0;
         int ge = 0;
         // Expands half (k 64*half .. +63) of this thread's weight row for the next
-        // group of the walk.
-        auto expand = [&]() -> bool {
+        // group of the walk and stores it into the TMEM weight tile; the caller
+        // publishes it (wait::st, fence, arrival on aready) with its own stores.
+        uint32_t a_pub = 0;  // the tile the last expansion wrote
+        auto expand_issue = [&]() -> bool {
             const uint32_t s = sde % kStages, a = jd % kABufs, ua = jd / kABufs;
-            const bool w_ok = ab.wait(full + s, (sde / kStages) & 1) && ab.wait(aempty + a, (ua & 1) ^ 1);
+            const bool w_ok = ab.wait(full + s, (sde / kStages) & 1) && ab.wait(gdone + a, (ua & 1) ^ 1);
             if (!__all_sync(kFull, w_ok)) return false;
             // Packed row lrow of the group: 64 bytes, 16-byte chunks swizzled by (row/2)%4.
             // A stage holds [kSG groups][128 rows][64 B]; for SWIGLU it holds two such
@@ -412,13 +412,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     expand_lo(c1.x), expand_hi(c1.x), expand_lo(c1.y), expand_hi(c1.y),
                                     expand_lo(c1.z), expand_hi(c1.z), expand_lo(c1.w), expand_hi(c1.w)};
             tmem_st16(tmem + lane_off + kTmemA + a * 32 + half * 16, v);
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) arrive_cluster(aready_rank0 + a * 8);
+            a_pub = a;
             ++jd;
             if (ge % kSG == kSG - 1 || ge == kg - 1) ++sde;
             if (++ge == kg) ge = 0;
+            return true;
+        };
+        auto expand = [&]() -> bool {
+            if (!expand_issue()) return false;
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) arrive_cluster(aready_rank0 + a_pub * 8);
             return true;
         };
         bool ok = true;
@@ -458,10 +463,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             // One group: expand the weights of group j + kLead, then wait for this
             // group's accumulator, read it (re-arming the bias) and do the scale step.
             auto group = [&](int g, float sc_raw) -> bool {
-                if (jd < total && !expand()) return false;
-                const uint32_t b = j % kDBufs, v = j / kDBufs;
+                const bool exp = jd < total;
+                if (exp && !expand_issue()) return false;
+                const uint32_t b = j % kDBufs;
+                const bool w_ok = ab.wait(gdone + j % kABufs, (j / kABufs) & 1);
                 ++j;
-                const bool w_ok = ab.wait(accf + b, v & 1);
                 if (!__all_sync(kFull, w_ok)) return false;
                 tc_fence_after();
                 const float sc = sc_raw * 0.0625f;  // the expansion's factor 16
@@ -472,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t ta = d_base + b * kTok + hh * 32;
                     tmem_ld32(ta, r);
                     tmem_wait_ld();
-                    tmem_bias32(ta);
+                    tmem_bias32(ta);  // re-armed; waited for with the weight tile below
                     if (DOTS) {
                         if (row_ok) {
 #pragma unroll
@@ -491,10 +497,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
+                // one wait::st and fence publish the weight tile and the re-armed accumulator
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) arrive_cluster(acce_rank0 + b * 8);
+                if (lane == 0) {
+                    if (exp) arrive_cluster(aready_rank0 + a_pub * 8);
+                    arrive_cluster(acce_rank0 + b * 8);
+                }
                 return true;
             };
             // Scales run four groups ahead of their use (an L2 round trip is several
