@@ -158,6 +158,9 @@ def time_graph(torch, fn, steps, warmup, sync_all=None):
     return e0.elapsed_time(e1) / steps, g
 
 
+C3_CALLS = 4  # lm_head calls per captured graph in the C3 timing
+
+
 class Sweep:
     """The decode-projection sweep: 24 layers x 6 shapes of distinct weights."""
 
@@ -275,46 +278,67 @@ def run_extras(torch, ops, dev, steps, warmup, world, rank, dist):
     key = torch.empty(1, dtype=torch.int64, device=dev)
     tok = torch.empty(1, dtype=torch.int32, device=dev)
 
-    comm = None
+    comm = xchg = None
     if world > 1:
-        # the library's own NCCL communicator (w4a8_lmhead_argmax_allreduce)
+        # the library's own NCCL communicator (w4a8_lmhead_argmax_allreduce), and the
+        # peer-memory exchange buffers (w4a8_lmhead_argmax_xchg)
         store = dist.distributed_c10d._get_default_store()
         if rank == 0:
             store.set("w4a8_nccl_uid", ops.nccl_unique_id())
         comm = ops.NcclComm(world, store.get("w4a8_nccl_uid"), rank)
+        xchg = ops.PeerExchange()
 
     def c3():
-        if comm is None:
+        if xchg is None:
             ops.lmhead_argmax(w, xq, xs, act=ops.ACT_TOKEN, row_offset=0, workspace=wsp, best_key=key, tok=tok)
         else:
-            ops.lmhead_argmax_allreduce(w, xq, xs, comm, act=ops.ACT_TOKEN, row_offset=rank * per_rank,
-                                        workspace=wsp, best_key=key, tok=tok)
+            ops.lmhead_argmax_xchg(w, xq, xs, xchg, act=ops.ACT_TOKEN, row_offset=rank * per_rank,
+                                   workspace=wsp, best_key=key, tok=tok)
 
-    if world > 1:
+    def c3_nccl():
+        ops.lmhead_argmax_allreduce(w, xq, xs, comm, act=ops.ACT_TOKEN, row_offset=rank * per_rank,
+                                    workspace=wsp, best_key=key, tok=tok)
+
+    def max_ms(ms):
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # every rank replays its own graph (C3_CALLS tokens' lm_head calls, chained by
+    # programmatic dependent launch as in a captured decode loop); the exchange
+    # kernel meets the other ranks once per call
+    ms, g = time_graph(torch, lambda: [c3() for _ in range(C3_CALLS)], steps, warmup,
+                       (lambda: dist.barrier()) if world > 1 else None)
+    del g
+    ms = max_ms(ms) / C3_CALLS
+    ms_nccl = None
+    if comm is not None:
         # NCCL collectives stay eager (no graph capture across ranks here)
         for _ in range(warmup):
-            c3()
+            c3_nccl()
         torch.cuda.synchronize()
         dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
-            c3()
+            c3_nccl()
         e1.record()
         torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / steps
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    else:
-        ms, g = time_graph(torch, c3, steps, warmup)
-        del g
+        ms_nccl = max_ms(e0.elapsed_time(e1) / steps)
     lm_bytes = gemv_bytes(k, vocab)
     out["c3_lmhead_argmax"] = {"gpus": world, "us_per_token": round(ms * 1e3, 2), "tok_s": round(1e3 / ms, 1),
                                "gbs_total": round(lm_bytes / (ms * 1e-3) / 1e9, 1),
                                "frac_hbm_per_gpu": round(lm_bytes / world / (ms * 1e-3) / 1e9 / hbm, 3),
-                               "collective": "w4a8_lmhead_argmax_allreduce: NCCL all-reduce (max, u64) of the "
-                                             "packed keys" if world > 1 else None}
+                               "collective": "w4a8_lmhead_argmax_xchg: packed keys stored into every peer's "
+                                             "buffer over NVLink, one flag per rank, in one kernel"
+                                             if world > 1 else None,
+                               "us_per_token_nccl_allreduce": round(ms_nccl * 1e3, 2) if ms_nccl else None,
+                               "timing": f"CUDA graph of {C3_CALLS} calls (one token each), PDL between them"}
+    if xchg is not None:
+        dist.barrier()  # no rank frees its buffer while a peer may still store into it
+        xchg.close()
     if comm is not None:
         comm.close()
     del w

@@ -200,6 +200,40 @@ W4A8_API w4a8_status w4a8_nccl_get_unique_id(void* id_out);
 W4A8_API w4a8_status w4a8_nccl_comm_init(int32_t nranks, const void* id, int32_t rank, void** comm_out);
 W4A8_API w4a8_status w4a8_nccl_comm_destroy(void* comm);
 
+/* Peer-memory key exchange for the column-split lm_head, the alternative to the
+ * NCCL all-reduce above for ranks of one node (one process per GPU, GPUs that can
+ * reach each other's memory over NVLink).  Each rank owns a small exchange buffer
+ * in its GPU memory; every rank opens every other rank's buffer through a CUDA IPC
+ * handle (W4A8_XCHG_HANDLE_BYTES bytes, passed between the processes by the host,
+ * e.g. an all-gather over torch.distributed).  A call then runs the shard's
+ * lm_head argmax and one exchange kernel: it stores the rank's keys into every
+ * peer's buffer, raises its per-call sequence flag there, waits (bounded) for all
+ * ranks' flags and takes the max, so every rank gets the key and token of the
+ * global argmax, bit-identical to one GPU, without NCCL.  The key slots are
+ * double-buffered by the sequence's parity and the sequence counter lives on the
+ * device, so the calls can be captured in a CUDA graph; every rank must make the
+ * same number of calls with the same m (<= W4A8_XCHG_MAX_TOKENS).  A wait that
+ * gives up leaves this rank's own keys in best_key and sets the device error word
+ * (w4a8_device_error reports W4A8_ETIMEOUT).  No counterpart in the reference (the
+ * exchange step of its sharded head, survey row (e), done over peer memory). */
+#define W4A8_XCHG_HANDLE_BYTES 64
+#define W4A8_XCHG_MAX_RANKS 8
+#define W4A8_XCHG_MAX_TOKENS 16
+typedef struct w4a8_xchg w4a8_xchg;
+/* Allocates this rank's exchange buffer on the current device (rank in
+ * [0, world), world <= W4A8_XCHG_MAX_RANKS) and writes its IPC handle. */
+W4A8_API w4a8_status w4a8_xchg_create(int32_t world, int32_t rank, void* handle_out, w4a8_xchg** out);
+/* Opens the peers' buffers: handles holds world handles of W4A8_XCHG_HANDLE_BYTES
+ * bytes in rank order (this rank's own entry is not used). */
+W4A8_API w4a8_status w4a8_xchg_open(w4a8_xchg* x, const void* handles);
+W4A8_API w4a8_status w4a8_xchg_destroy(w4a8_xchg* x);
+/* As w4a8_lmhead_argmax_allreduce, with the exchange over x instead of NCCL. */
+W4A8_API w4a8_status w4a8_lmhead_argmax_xchg(const w4a8_weight* w, int32_t row_offset, const int8_t* xq,
+                                            const float* xs, int32_t act, int32_t m, float* logits,
+                                            uint64_t* best_key, uint32_t* tok_out, const uint32_t* ids,
+                                            void* workspace, size_t workspace_bytes, w4a8_xchg* x,
+                                            void* stream);
+
 /* Index carried by a packed argmax key (0 for the "no value > -3e38" key 0). */
 static inline uint32_t w4a8_key_index(uint64_t key) {
     return key ? ~(uint32_t)(key & 0xffffffffu) : 0u;

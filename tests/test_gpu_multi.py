@@ -1,7 +1,9 @@
 """The column-split lm_head on 2 GPUs (one rank per GPU): each rank holds half of
 the vocabulary rows and the keys are exchanged (a) through torch.distributed NCCL
-(ops.lmhead_argmax_sharded) and (b) inside the library (w4a8_lmhead_argmax_allreduce
-over its own NCCL communicator).  Both must give the one-device argmax of the
+(ops.lmhead_argmax_sharded), (b) inside the library (w4a8_lmhead_argmax_allreduce
+over its own NCCL communicator) and (c) over peer memory (w4a8_lmhead_argmax_xchg:
+three calls, so both halves of the double-buffered key slots are used, then two
+replays of a captured CUDA graph).  All must give the one-device argmax of the
 oracle bit for bit, on every rank.  Skipped with fewer than 2 GPUs."""
 
 import datetime
@@ -63,7 +65,36 @@ def _rank(rank, world, port, results):
     key2, tok2 = ops.lmhead_argmax_allreduce(w, xq_d, xs_d, comm, act=ops.ACT_TOKEN, row_offset=lo)
     torch.cuda.synchronize()
     comm.close()
-    results[rank] = (key1.tolist(), tok1.tolist(), key2.tolist(), tok2.tolist())
+    xchg = ops.PeerExchange()
+    ws = ops.lmhead_workspace(w, M, dev)
+    key3 = torch.empty(M, dtype=torch.int64, device=dev)
+    tok3 = torch.empty(M, dtype=torch.int32, device=dev)
+    got3 = []
+    for _ in range(3):
+        key3.zero_()
+        tok3.zero_()
+        ops.lmhead_argmax_xchg(w, xq_d, xs_d, xchg, act=ops.ACT_TOKEN, row_offset=lo, workspace=ws, best_key=key3,
+                               tok=tok3)
+        torch.cuda.synchronize()
+        got3.append((key3.tolist(), tok3.tolist()))
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            ops.lmhead_argmax_xchg(w, xq_d, xs_d, xchg, act=ops.ACT_TOKEN, row_offset=lo, workspace=ws,
+                                   best_key=key3, tok=tok3)
+    for _ in range(2):
+        key3.zero_()
+        tok3.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        got3.append((key3.tolist(), tok3.tolist()))
+    err = ops.device_error()
+    del g
+    dist.barrier()  # no rank closes its buffer while a peer may still store into it
+    xchg.close()
+    results[rank] = (key1.tolist(), tok1.tolist(), key2.tolist(), tok2.tolist(), got3, err)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -81,6 +112,9 @@ def test_lmhead_split_two_gpus(cuda):
     ref_tok = orc.argmax(logits).astype(np.int64).tolist()
     ref_key = [to_i64(shard_key(row, 0)) for row in logits]
     for r in range(world):
-        key1, tok1, key2, tok2 = got[r]
+        key1, tok1, key2, tok2, got3, err = got[r]
         assert key1 == ref_key and key2 == ref_key, r
         assert tok1 == ref_tok and tok2 == ref_tok, r
+        assert err == 0, r
+        for i, (key3, tok3) in enumerate(got3):
+            assert key3 == ref_key and tok3 == ref_tok, (r, i)

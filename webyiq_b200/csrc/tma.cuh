@@ -13,6 +13,7 @@ enum : unsigned int {
     DEV_ERR_TMA_TIMEOUT = 1u,   // GEMV: a weight copy never landed
     DEV_ERR_GEMM_TIMEOUT = 2u,  // GEMM: a pipeline wait gave up
     DEV_ERR_SELFTEST = 4u,      // w4a8_selftest_wait_timeout: its wait gave up (as it must)
+    DEV_ERR_XCHG_TIMEOUT = 8u,  // peer key exchange: a rank's flag never arrived
 };
 
 // --- TMA bulk copies and mbarriers (no cluster multicast anywhere) -----------

@@ -215,6 +215,53 @@ def lmhead_argmax_sharded(w, xq, xs, row_offset, act=ACT_TOKEN, group=None, ids=
     return best_key, keys_to_tokens(best_key, ids)
 
 
+XCHG_HANDLE_BYTES = 64
+
+
+class PeerExchange:
+    """Peer-memory exchange buffers for w4a8_lmhead_argmax_xchg (one process per GPU
+    of one node): this rank's buffer is made on the current device and its CUDA IPC
+    handle is all-gathered over the torch.distributed group, then every peer's buffer
+    is opened.  Every rank of the group must construct it (collective)."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.ptr = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(XCHG_HANDLE_BYTES)
+        _lib.check(_lib.load().w4a8_xchg_create(self.world, self.rank, handle, ctypes.byref(self.ptr)))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle.raw), group=group)
+        allh = ctypes.create_string_buffer(b"".join(handles), XCHG_HANDLE_BYTES * self.world)
+        _lib.check(_lib.load().w4a8_xchg_open(self.ptr, allh))
+
+    def close(self):
+        if self.ptr:
+            _lib.check(_lib.load().w4a8_xchg_destroy(self.ptr))
+            self.ptr = ctypes.c_void_p()
+
+
+def lmhead_argmax_xchg(w, xq, xs, xchg, act=ACT_TOKEN, row_offset=0, logits=None, ids=None, workspace=None,
+                       best_key=None, tok=None):
+    """Sharded lm_head with the key exchange over peer memory (PeerExchange) instead
+    of NCCL.  Returns (best_key int64 [m], tok int32 [m]) of the global argmax."""
+    _need_cuda(xq, xs, logits, ids, workspace)
+    m = xq.shape[0]
+    dev = xq.device
+    if workspace is None:
+        workspace = lmhead_workspace(w, m, dev)
+    if best_key is None:
+        best_key = torch.empty(m, dtype=torch.int64, device=dev)
+    if tok is None:
+        tok = torch.empty(m, dtype=torch.int32, device=dev)
+    _lib.check(_lib.load().w4a8_lmhead_argmax_xchg(ctypes.byref(w.c), int(row_offset), _ptr(xq), _ptr(xs), act, m,
+                                                   _ptr(logits), _ptr(best_key), _ptr(tok), _ptr(ids),
+                                                   _ptr(workspace), workspace.numel(), xchg.ptr, _stream()))
+    return best_key, tok
+
+
 def nccl_unique_id():
     """128-byte NCCL unique id (make it on one rank, give it to all)."""
     buf = ctypes.create_string_buffer(128)
