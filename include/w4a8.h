@@ -125,6 +125,15 @@ W4A8_API w4a8_status w4a8_gemv(const w4a8_weight* w, const int8_t* xq, const flo
 W4A8_API w4a8_status w4a8_gemv_x(const w4a8_weight* w, const float* x, int32_t m, int32_t mode, float* y,
                                  void* stream);
 
+/* The norm_quant prologue of a decode block fused as well: RMSNorm with weights
+ * norm_w f32[k] and eps, per-token quantization and the GEMV in one launch
+ * (graph.rs:266,323 norm_quant then Builder::gemv; quant.wgsl:19-62 with NORM).
+ * Bit-identical to w4a8_quant(x, norm_w, eps, m, k, W4A8_ACT_TOKEN) followed by
+ * w4a8_gemv.  Group-128 weights, m in [1, 2] tokens (the decode and MTP-verify
+ * widths); W4A8_ENOTSUP for other calls. */
+W4A8_API w4a8_status w4a8_gemv_xn(const w4a8_weight* w, const float* x, const float* norm_w, float eps, int32_t m,
+                                 int32_t mode, float* y, void* stream);
+
 /* Prefill GEMM Y[m, n] = X W^T for any m >= 1 (gemm_q4q8.wgsl:46-121,
  * Builder::gemm graph.rs:200-205).  Group-128 symmetric weights with
  * W4A8_ACT_TOKEN run on the tcgen05 tensor cores (int4 expanded to int8 in shared

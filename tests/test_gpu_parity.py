@@ -389,6 +389,45 @@ def test_gemv_decode_shapes(cuda, n, k, m, mode, has_min, fq):
     assert ops.device_error() == 0
 
 
+@pytest.mark.parametrize("has_min", [False, True])
+@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("n,k", [(6144, 2048), (2048, 6144), (2048, 4096), (600, 384), (1500, 2560), (2960, 8192)])
+def test_gemv_norm_quant_fused(cuda, n, k, m, mode, has_min):
+    """w4a8_gemv_xn (RMSNorm + per-token quant + GEMV in one launch) equals
+    w4a8_quant(norm) followed by w4a8_gemv bit for bit, and the oracle (bit-exact;
+    SWIGLU within 1e-3), a zero row included; more than two tokens, and two tokens
+    with more than 32 groups a row, are refused."""
+    q, s, _ = make_weight(n, k, 128, has_min, seed=n + k + 3 * m + mode)
+    x = make_x(m, k, seed=k + m + 7)
+    if m == 2 and has_min:
+        x[1] = 0.0
+    nw = (1 + 0.3 * make_x(1, k, seed=9)[0]).astype(np.float32)
+    eps = 1e-6
+    xq, xs = orc.quant(x, nw, eps, act=1)
+    n_out = n // 2 if mode == 2 else n
+    y0 = make_x(m, n_out, seed=8) if mode == 1 else None
+    ref = orc.gemv(q, s, k, 128, has_min, xq, xs, act=1, mode=mode, y=None if y0 is None else y0.copy())
+    w = dev_weight(q, s, n, k, 128, has_min, cuda)
+    base = lambda: None if y0 is None else to_dev(y0, cuda)  # noqa: E731
+    if m == 2 and k > 4096:  # two tokens: at most 32 groups a row (the decode kernel's cover)
+        with pytest.raises(W4A8Error):
+            ops.gemv_xn(w, to_dev(x, cuda), to_dev(nw, cuda), eps, mode=mode, y=base())
+        return
+    y = ops.gemv_xn(w, to_dev(x, cuda), to_dev(nw, cuda), eps, mode=mode, y=base())
+    xq_d, xs_d = ops.quant(to_dev(x, cuda), to_dev(nw, cuda), eps, act=1)
+    y2 = ops.gemv(w, xq_d, xs_d, act=1, mode=mode, y=base())
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(bits(y.cpu().numpy()), bits(y2.cpu().numpy()))
+    if mode == 2:
+        assert_rel_close(y.cpu().numpy(), ref, 1e-3)
+    else:
+        np.testing.assert_array_equal(bits(y.cpu().numpy()), bits(ref))
+    if m == 1 and mode == 0:
+        with pytest.raises(W4A8Error):
+            ops.gemv_xn(w, to_dev(make_x(4, k), cuda), to_dev(nw, cuda), eps)
+
+
 def test_gemv_fused_quant_rejects_group32(cuda):
     q, s, _ = make_weight(32, 256, 32, True, seed=1)
     w = dev_weight(q, s, 32, 256, 32, True, cuda)

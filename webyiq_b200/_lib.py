@@ -37,6 +37,7 @@ _SIGS = {
     "w4a8_gemv": (ctypes.c_int, [ctypes.POINTER(Weight), _P, _P, _I, _I, _I, _P, _P]),
     "w4a8_gemm": (ctypes.c_int, [ctypes.POINTER(Weight), _P, _P, _I, _I, _I, _P, _P]),
     "w4a8_gemv_x": (ctypes.c_int, [ctypes.POINTER(Weight), _P, _I, _I, _P, _P]),
+    "w4a8_gemv_xn": (ctypes.c_int, [ctypes.POINTER(Weight), _P, _P, ctypes.c_float, _I, _I, _P, _P]),
     "w4a8_matmul": (ctypes.c_int, [ctypes.POINTER(Weight), _P, _P, _I, _I, _I, _P, _P]),
     "w4a8_argmax": (ctypes.c_int, [_P, _I, _I, _P, _P, _P]),
     "w4a8_lmhead_argmax": (ctypes.c_int, [ctypes.POINTER(Weight), _I, _P, _P, _I, _I, _P, _P, _P, _P, _P,

@@ -202,6 +202,33 @@ w4a8_status w4a8_gemv_x(const w4a8_weight* w, const float* x, int32_t m, int32_t
     return launch_gemv_mma(p, w->has_min != 0, mode, OUT_Y, static_cast<cudaStream_t>(stream));
 }
 
+w4a8_status w4a8_gemv_xn(const w4a8_weight* w, const float* x, const float* norm_w, float eps, int32_t m, int32_t mode,
+                         float* y, void* stream) {
+    w4a8_status st = check_weight(w, "w4a8_gemv_xn");
+    if (st != W4A8_OK) return st;
+    if (w->group != 128) return set_error(W4A8_ENOTSUP, "w4a8_gemv_xn: group-128 weights only (group %d)", w->group);
+    if (!x || !aligned(x, 16)) return set_error(W4A8_EINVAL, "w4a8_gemv_xn: x NULL or not 16-byte aligned");
+    if (!norm_w || !aligned(norm_w, 16)) return set_error(W4A8_EINVAL, "w4a8_gemv_xn: norm_w NULL or not 16-byte aligned");
+    if (!y) return set_error(W4A8_EINVAL, "w4a8_gemv_xn: y is NULL");
+    if (m < 1 || m > 2) return set_error(W4A8_ENOTSUP, "w4a8_gemv_xn: m=%d (1 or 2 tokens)", m);
+    if (mode < W4A8_STORE || mode > W4A8_SWIGLU) return set_error(W4A8_EINVAL, "w4a8_gemv_xn: mode=%d", mode);
+    if (mode == W4A8_SWIGLU && w->n % 2) return set_error(W4A8_EINVAL, "w4a8_gemv_xn: SWIGLU needs even n (%d)", w->n);
+    GemvParams p{};
+    p.q = static_cast<const uint4*>(w->q);
+    p.s = w->s;
+    p.xf32 = x;
+    p.norm_w = norm_w;
+    p.eps = eps;
+    p.y = y;
+    p.n_out = mode == W4A8_SWIGLU ? w->n / 2 : w->n;
+    p.y_stride = p.n_out;
+    p.k = w->k;
+    p.m = m;
+    if (!gemv_dec_covers(p, 128, W4A8_ACT_TOKEN, mode, OUT_Y))
+        return set_error(W4A8_ENOTSUP, "w4a8_gemv_xn: n=%d k=%d outside the decode kernel's plan", w->n, w->k);
+    return launch_gemv_dec(p, w->has_min != 0, mode, static_cast<cudaStream_t>(stream));
+}
+
 w4a8_status w4a8_group_dots(const w4a8_weight* w, const int8_t* xq, int32_t m, int32_t* dots, void* stream) {
     w4a8_status st = check_weight(w, "w4a8_group_dots");
     if (st != W4A8_OK) return st;

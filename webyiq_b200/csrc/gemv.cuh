@@ -51,6 +51,8 @@ struct GemvParams {
     const int8_t* xq;      // [m, k]
     const float* xs;       // [m] (TOKEN) or [m, k/32, 2] (GROUP32)
     const float* xf32;     // tensor-core GEMV only: [m, k] f32 activations quantized per token inside
+    const float* norm_w;   // decode GEMV with fused quant only: RMSNorm weights [k] (or null)
+    float eps;             // and its epsilon
     float* y;              // OUT_Y: output; OUT_ARGMAX: logits or null
     int* dots;             // OUT_DOTS: [m, n_out, k/G]
     unsigned int* counter;           // OUT_ARGMAX workspace: CTAs done

@@ -58,6 +58,8 @@ struct DecParams {
     const int8_t* xq;        // [m][k]
     const float* xs;         // [m] per-token dx
     const float* xf32;       // [m][k] f32 activations to quantize here (FQ), else null
+    const float* nw;         // FQ with NORM: RMSNorm weights [k]
+    float eps;
     float* y;                // [m][y_stride]
     int n_out, k, m, y_stride;
     int L;         // lanes per row
@@ -71,7 +73,7 @@ __device__ __forceinline__ int pack_fix(uint32_t h) {
     return (f.mant << 8) | f.sh;
 }
 
-template <bool HAS_MIN, int MODE, int MT, int GPL, bool FQ>
+template <bool HAS_MIN, int MODE, int MT, int GPL, bool FQ, bool NORM>
 __global__ void __launch_bounds__(DecThreads<MT, GPL>::value, 2) gemv_dec_kernel(const DecParams p) {
     constexpr bool SWI = MODE == W4A8_SWIGLU;
     constexpr int NH = SWI ? 2 : 1;  // weight rows per output row (gate, up)
@@ -187,18 +189,65 @@ __global__ void __launch_bounds__(DecThreads<MT, GPL>::value, 2) gemv_dec_kernel
         // registers across the amax exchange.  A warp's 32 neighbouring float4s are
         // one 128-group, so the group sums come from warp shuffles.
         constexpr int VPT = MT == 1 ? kDecVPT : kDecVPT / 2;
+        // With the norm, the first 256 threads hold x as the quant kernel's 256
+        // threads do (float4 t + 256 j), so the sum of squares is added in the same
+        // order and the RMS scale has the same bits.
+        constexpr int XS = NORM ? 256 : T;  // stride of a thread's float4s
+        const bool holder = !NORM || tid < 256;
         float4 v[MT][VPT];
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
-            float a = 0.0f;
             const float4* src = reinterpret_cast<const float4*>(p.xf32 + static_cast<size_t>(t) * K);
 #pragma unroll
             for (int u = 0; u < VPT; ++u) {
-                const int i = tid + u * T;
+                const int i = tid + u * XS;
                 v[t][u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (t < p.m && i < K / 4) v[t][u] = __ldg(src + i);
-                a = fmaxf(fmaxf(a, fabsf(v[t][u].x)), fmaxf(fmaxf(fabsf(v[t][u].y), fabsf(v[t][u].z)), fabsf(v[t][u].w)));
+                if (holder && t < p.m && i < K / 4) v[t][u] = __ldg(src + i);
             }
+        }
+        if (NORM) {
+            // scale = 1 / sqrt(sum(x^2) / k + eps): per-thread fma chain in element
+            // order, a butterfly within each warp, then the 8 warp totals in order
+            __shared__ float s_ss[2][8];
+#pragma unroll
+            for (int t = 0; t < MT; ++t) {
+                float ss = 0.0f;
+#pragma unroll
+                for (int u = 0; u < VPT; ++u) {
+                    ss = __fmaf_rn(v[t][u].x, v[t][u].x, ss);
+                    ss = __fmaf_rn(v[t][u].y, v[t][u].y, ss);
+                    ss = __fmaf_rn(v[t][u].z, v[t][u].z, ss);
+                    ss = __fmaf_rn(v[t][u].w, v[t][u].w, ss);
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(kFull, ss, off));
+                if (lane == 0 && warp < 8) s_ss[t][warp] = ss;
+            }
+            __syncthreads();
+#pragma unroll
+            for (int t = 0; t < MT; ++t) {
+                float tot = 0.0f;
+                for (int w8 = 0; w8 < 8; ++w8) tot = __fadd_rn(tot, s_ss[t][w8]);
+                const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(K)), p.eps)));
+                const float4* nw4 = reinterpret_cast<const float4*>(p.nw);
+#pragma unroll
+                for (int u = 0; u < VPT; ++u) {
+                    const int i = tid + u * XS;
+                    if (!holder || t >= p.m || i >= K / 4) continue;
+                    const float4 n = __ldg(nw4 + i);
+                    v[t][u].x = __fmul_rn(__fmul_rn(v[t][u].x, sc), n.x);
+                    v[t][u].y = __fmul_rn(__fmul_rn(v[t][u].y, sc), n.y);
+                    v[t][u].z = __fmul_rn(__fmul_rn(v[t][u].z, sc), n.z);
+                    v[t][u].w = __fmul_rn(__fmul_rn(v[t][u].w, sc), n.w);
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+            float a = 0.0f;
+#pragma unroll
+            for (int u = 0; u < VPT; ++u)
+                a = fmaxf(fmaxf(a, fabsf(v[t][u].x)), fmaxf(fmaxf(fabsf(v[t][u].y), fabsf(v[t][u].z)), fabsf(v[t][u].w)));
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(kFull, a, off));
             if (lane == 0 && t < p.m) atomicMax(&s_amax[t], __float_as_uint(a));
@@ -211,14 +260,14 @@ __global__ void __launch_bounds__(DecThreads<MT, GPL>::value, 2) gemv_dec_kernel
             const float inv = a > 0.0f ? __fdiv_rn(1.0f, __fdiv_rn(a, 127.0f)) : 0.0f;
 #pragma unroll
             for (int u = 0; u < VPT; ++u) {
-                const int i = tid + u * T;  // float4 index: elements 4i..4i+3
-                if (u * T >= K / 4) break;   // warp-uniform (K / 4 is a multiple of 32)
+                const int i = tid + u * XS;  // float4 index: elements 4i..4i+3
+                if (u * XS >= K / 4) break;   // warp-uniform (K / 4 is a multiple of 32)
                 const int q0 = static_cast<int>(rintf(__fmul_rn(v[t][u].x, inv)));
                 const int q1 = static_cast<int>(rintf(__fmul_rn(v[t][u].y, inv)));
                 const int q2 = static_cast<int>(rintf(__fmul_rn(v[t][u].z, inv)));
                 const int q3 = static_cast<int>(rintf(__fmul_rn(v[t][u].w, inv)));
                 int X = 0;
-                if (i < K / 4) {
+                if (holder && i < K / 4) {
                     *reinterpret_cast<uint32_t*>(xhalf(t, (i >> 2) & 1, i >> 3) + (i & 3) * 4) =
                         (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
                         ((static_cast<uint32_t>(q2) & 0xffu) << 16) | ((static_cast<uint32_t>(q3) & 0xffu) << 24);
@@ -226,7 +275,7 @@ __global__ void __launch_bounds__(DecThreads<MT, GPL>::value, 2) gemv_dec_kernel
                 }
 #pragma unroll
                 for (int off = 16; off > 0; off >>= 1) X += __shfl_xor_sync(kFull, X, off);
-                if (lane == 0 && i < K / 4) xgrp(t)[i >> 5] = X;
+                if (lane == 0 && holder && i < K / 4) xgrp(t)[i >> 5] = X;
             }
             if (tid == 0) s_dx[t] = __fdiv_rn(a, 127.0f);
         }
@@ -371,14 +420,15 @@ bool dec_plan(const GemvParams& g, bool has_min, int mode, DecPlan& pl) {
               (g.xf32 ? static_cast<size_t>(g.m) * (g.k + (((g.k / 128) * 4 + 15) & ~15)) : 0);  // fused quant staging
     const int rows_per_pass = (pl.threads / 32) * (32 / pl.sh.L);
     const int npass = (pl.rows_max + rows_per_pass - 1) / rows_per_pass;
-    const bool vpt_ok = !g.xf32 || (g.k / 4 + pl.threads - 1) / pl.threads <= (g.m == 1 ? kDecVPT : kDecVPT / 2);
+    const int xs = g.norm_w ? 256 : pl.threads;  // the threads that hold x (the norm's partition)
+    const bool vpt_ok = !g.xf32 || (g.k / 4 + xs - 1) / xs <= (g.m == 1 ? kDecVPT : kDecVPT / 2);
     return pl.smem <= kDecSmemBudget && npass <= kDecMaxPass && vpt_ok;
 }
 
-template <bool HAS_MIN, int MODE, int MT, int GPL, bool FQ>
+template <bool HAS_MIN, int MODE, int MT, int GPL, bool FQ, bool NORM>
 w4a8_status dec_inst(const DecParams& p, const DecPlan& pl, cudaStream_t st) {
     static size_t configured = 0;  // set on first use: static shared memory counts against the default 48 KB too
-    auto kernel = gemv_dec_kernel<HAS_MIN, MODE, MT, GPL, FQ>;
+    auto kernel = gemv_dec_kernel<HAS_MIN, MODE, MT, GPL, FQ, NORM>;
     if (pl.smem > configured) {
         const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pl.smem));
         if (e != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8 gemv (decode): smem attribute: %s", cudaGetErrorString(e));
@@ -387,17 +437,19 @@ w4a8_status dec_inst(const DecParams& p, const DecPlan& pl, cudaStream_t st) {
     return launch_pdl("w4a8 gemv (decode)", kernel, dim3(pl.ctas), dim3(DecThreads<MT, GPL>::value), pl.smem, st, p);
 }
 
-template <bool HAS_MIN, int MODE, bool FQ>
+template <bool HAS_MIN, int MODE, bool FQ, bool NORM>
 w4a8_status dec_shape_dispatch(const DecParams& p, const DecPlan& pl, cudaStream_t st) {
-    if (p.m == 1) return pl.sh.gpl == 1 ? dec_inst<HAS_MIN, MODE, 1, 1, FQ>(p, pl, st) : dec_inst<HAS_MIN, MODE, 1, 2, FQ>(p, pl, st);
-    return dec_inst<HAS_MIN, MODE, 2, 1, FQ>(p, pl, st);
+    if (p.m == 1)
+        return pl.sh.gpl == 1 ? dec_inst<HAS_MIN, MODE, 1, 1, FQ, NORM>(p, pl, st)
+                              : dec_inst<HAS_MIN, MODE, 1, 2, FQ, NORM>(p, pl, st);
+    return dec_inst<HAS_MIN, MODE, 2, 1, FQ, NORM>(p, pl, st);
 }
 
-template <bool HAS_MIN, bool FQ>
+template <bool HAS_MIN, bool FQ, bool NORM = false>
 w4a8_status dec_mode_dispatch(const DecParams& p, const DecPlan& pl, int mode, cudaStream_t st) {
-    if (mode == W4A8_STORE) return dec_shape_dispatch<HAS_MIN, W4A8_STORE, FQ>(p, pl, st);
-    if (mode == W4A8_ADD) return dec_shape_dispatch<HAS_MIN, W4A8_ADD, FQ>(p, pl, st);
-    return dec_shape_dispatch<HAS_MIN, W4A8_SWIGLU, FQ>(p, pl, st);
+    if (mode == W4A8_STORE) return dec_shape_dispatch<HAS_MIN, W4A8_STORE, FQ, NORM>(p, pl, st);
+    if (mode == W4A8_ADD) return dec_shape_dispatch<HAS_MIN, W4A8_ADD, FQ, NORM>(p, pl, st);
+    return dec_shape_dispatch<HAS_MIN, W4A8_SWIGLU, FQ, NORM>(p, pl, st);
 }
 
 }  // namespace
@@ -419,6 +471,8 @@ w4a8_status launch_gemv_dec(const GemvParams& g, bool has_min, int mode, cudaStr
     p.xq = g.xq;
     p.xs = g.xs;
     p.xf32 = g.xf32;
+    p.nw = g.norm_w;
+    p.eps = g.eps;
     p.y = g.y;
     p.n_out = g.n_out;
     p.k = g.k;
@@ -428,6 +482,9 @@ w4a8_status launch_gemv_dec(const GemvParams& g, bool has_min, int mode, cudaStr
     p.rows_max = pl.rows_max;
     p.sc_off = pl.sc_off;
     p.sc_half = pl.sc_half;
+    if (g.xf32 && g.norm_w)
+        return has_min ? dec_mode_dispatch<true, true, true>(p, pl, mode, st)
+                       : dec_mode_dispatch<false, true, true>(p, pl, mode, st);
     if (g.xf32) return has_min ? dec_mode_dispatch<true, true>(p, pl, mode, st) : dec_mode_dispatch<false, true>(p, pl, mode, st);
     return has_min ? dec_mode_dispatch<true, false>(p, pl, mode, st) : dec_mode_dispatch<false, false>(p, pl, mode, st);
 }

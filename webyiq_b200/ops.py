@@ -94,6 +94,18 @@ def gemv_x(w, x, mode=STORE, y=None):
     return y
 
 
+def gemv_xn(w, x, norm_w, eps, mode=STORE, y=None):
+    """RMSNorm (norm_w f32 [k], eps), per-token quant and the GEMV in one launch, for
+    one or two tokens; equal to quant(x, norm_w, eps, act=ACT_TOKEN) followed by gemv,
+    bit for bit."""
+    _need_cuda(x, norm_w, y)
+    m = x.shape[0]
+    y = _out(w, m, mode, y, x.device)
+    _lib.check(_lib.load().w4a8_gemv_xn(ctypes.byref(w.c), _ptr(x), _ptr(norm_w), float(eps), m, mode, _ptr(y),
+                                        _stream()))
+    return y
+
+
 def gemm(w, xq, xs, act=ACT_GROUP32, mode=STORE, y=None):
     """Y (+)= X W^T for any m (gemm_q4q8.wgsl)."""
     _need_cuda(xq, xs, y)
