@@ -62,6 +62,31 @@ def test_cli_ref_matmul(cuda, cli, tmp_path, group, has_min, act):
             assert " 0 of " in out, out
 
 
+@pytest.mark.parametrize("norm", [False, True])
+def test_cli_ref_quant_gemv(cuda, cli, tmp_path, norm):
+    """Builder::quant_gemv: the norm_quant prologue and the projection in one launch,
+    through the C++ host, against the oracle's quant(norm) + gemv."""
+    n, k = 512, 2048
+    q, s, _ = make_weight(n, k, 128, False, seed=21)
+    d = str(tmp_path / "model")
+    fmt.write_model(d, {"blk.0.q.q": (q, "q4", (n, k)), "blk.0.q.s": (s, "f16", s.shape)}, group=128,
+                    scheme="sym-rtn")
+    nw = (1 + 0.2 * make_x(1, k, seed=4)[0]).astype(np.float32) if norm else None
+    for m in (1, 2):
+        for mode in (0, 1):
+            x = make_x(m, k, seed=m + 5 * mode)
+            xq, xs = orc.quant(x, nw, 1e-6, act=1)
+            y0 = make_x(m, n, seed=98) if mode == 1 else None
+            y = orc.gemv(q, s, k, 128, False, xq, xs, act=1, mode=mode, y=None if y0 is None else y0.copy())
+            prefix = str(tmp_path / f"qg_m{m}_mode{mode}")
+            _write_case(prefix, "quant_gemv", "blk.0.q", m, 1, mode, x, y=y, y0=y0)
+            if nw is not None:
+                nw.tofile(prefix + ".nw.f32")
+            rc, out = _run(cli, d, "--ref", prefix)
+            assert rc == 0, out
+            assert " 0 of " in out and "one launch" in out, out
+
+
 def test_cli_ref_lmhead_and_bench(cuda, cli, tmp_path):
     v, k = 4096, 512
     q, s, _ = make_weight(v, k, 128, False, seed=5)

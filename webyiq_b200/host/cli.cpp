@@ -5,13 +5,15 @@
 //   webyiq_cli <model_dir> --list
 //       tensors of the manifest (no GPU needed)
 //   webyiq_cli <model_dir> --ref <prefix>
-//       <prefix>.json {"op": "matmul" | "lm_head", "weight": name, "m": M,
+//       <prefix>.json {"op": "matmul" | "quant_gemv" | "lm_head", "weight": name, "m": M,
 //                      "act": "token" | "group32", "mode": 0 | 1 | 2, "eps": e}
 //       <prefix>.x.f32  activations f32 [M, K] (quantized on the GPU)
+//       <prefix>.nw.f32 (quant_gemv, optional) RMSNorm weights f32 [K]
 //       <prefix>.y0.f32 (mode 1 only) y before the call
-//       <prefix>.y.f32  expected y f32 [M, N] (matmul) or <prefix>.tok.u32 (lm_head)
-//       runs quant + matmul (or the fused lm_head argmax) through the Builder and
-//       checks |y - ref| <= 1e-3 |ref| + 1e-3 rms(ref) (tokens: exact); exit 0 / 1
+//       <prefix>.y.f32  expected y f32 [M, N] (matmul, quant_gemv) or <prefix>.tok.u32 (lm_head)
+//       runs quant + matmul, the fused (norm +) quant + GEMV, or the fused lm_head
+//       argmax through the Builder and checks |y - ref| <= 1e-3 |ref| + 1e-3 rms(ref)
+//       (tokens: exact); exit 0 / 1
 //   webyiq_cli <model_dir> --bench <iters>
 //       every q4 weight: GEMV (M = 1) and GEMM (M = 1024) timed with CUDA events,
 //       and all GEMVs as one captured decode-step graph
@@ -96,8 +98,18 @@ int reference(Engine& e, const std::string& prefix) {
     cudaStream_t st;
     CK(cudaStreamCreate(&st));
     Builder b(e);
-    s = b.quant("quant", k, eps, dx, nullptr, m, act, dxq, dxs);
-    if (!s.ok()) return fail(s);
+    float* dnw = nullptr;
+    if (op == "quant_gemv") {
+        // optional RMSNorm weights <prefix>.nw.f32 (f32 [k])
+        std::vector<float> nw;
+        if (read_array(prefix + ".nw.f32", nw, k)) {
+            CK(cudaMalloc(&dnw, static_cast<size_t>(k) * 4));
+            CK(cudaMemcpy(dnw, nw.data(), static_cast<size_t>(k) * 4, cudaMemcpyHostToDevice));
+        }
+    } else {
+        s = b.quant("quant", k, eps, dx, nullptr, m, act, dxq, dxs);
+        if (!s.ok()) return fail(s);
+    }
     int rc = 0;
     if (op == "lm_head") {
         uint64_t* dkey = nullptr;
@@ -134,7 +146,10 @@ int reference(Engine& e, const std::string& prefix) {
             CK(cudaMemcpy(dy, y0.data(), y0.size() * 4, cudaMemcpyHostToDevice));
         }
         const Path path = m == 1 ? Path::Decode : m <= W4A8_GEMV_MAX_M ? Path::Verify : Path::Prefill;
-        s = b.matmul(path, m, "matmul", wname, k, rows, mode, dxq, dxs, act, dy);
+        if (op == "quant_gemv")
+            s = b.quant_gemv("quant_gemv", wname, k, rows, mode, m, dx, dnw, eps, dy);
+        else
+            s = b.matmul(path, m, "matmul", wname, k, rows, mode, dxq, dxs, act, dy);
         if (!s.ok()) return fail(s);
         Plan p(b.take());
         s = p.run(st);
@@ -156,15 +171,18 @@ int reference(Engine& e, const std::string& prefix) {
         for (size_t i = 0; i < y.size(); ++i)
             bad += std::fabs(static_cast<double>(y[i]) - want[i]) > 1e-3 * std::fabs(static_cast<double>(want[i])) + 1e-3 * rms;
         const double rel = maxr > 0 ? maxd / maxr : maxd;
-        printf("matmul %s m=%u (%s): max |diff| / max |ref| = %.3e, cosine %.8f, %zu of %zu outside 1e-3\n",
-               wname.c_str(), m, path == Path::Prefill ? "gemm" : "gemv", rel, dot / (std::sqrt(na * nb) + 1e-30),
-               bad, y.size());
+        printf("%s %s m=%u (%s): max |diff| / max |ref| = %.3e, cosine %.8f, %zu of %zu outside 1e-3\n",
+               op.c_str(), wname.c_str(), m,
+               op == "quant_gemv" ? (dnw ? "norm + quant + gemv, one launch" : "quant + gemv, one launch")
+                                  : path == Path::Prefill ? "gemm" : "gemv",
+               rel, dot / (std::sqrt(na * nb) + 1e-30), bad, y.size());
         rc = (rel <= 1e-3 && bad == 0) ? 0 : 1;
     }
     cudaFree(dx);
     cudaFree(dxq);
     cudaFree(dxs);
     cudaFree(dy);
+    if (dnw) cudaFree(dnw);
     cudaStreamDestroy(st);
     return rc;
 }

@@ -225,6 +225,23 @@ Status Builder::quant(const std::string& name, uint32_t k, double eps, const flo
     return Status::Ok();
 }
 
+Status Builder::quant_gemv(const std::string& name, const std::string& wn, uint32_t k, uint32_t n, uint32_t mode,
+                          uint32_t t, const float* x, const float* norm, double eps, float* y) {
+    w4a8_weight wt;
+    Status s = w(wn, k, n, wt);
+    if (!s.ok()) return s;
+    if (wt.group != 128) return Status::Error(str("%s: quant_gemv needs group-128 weights (group %d)", name.c_str(), wt.group));
+    if (t < 1 || t > (norm ? 2u : static_cast<uint32_t>(W4A8_GEMV_MAX_M)))
+        return Status::Error(str("%s: quant_gemv tokens %u", name.c_str(), t));
+    ops_.push_back({name, [=](cudaStream_t st) {
+                        if (norm)
+                            return w4a8_gemv_xn(&wt, x, norm, static_cast<float>(eps), static_cast<int32_t>(t),
+                                                static_cast<int32_t>(mode), y, st);
+                        return w4a8_gemv_x(&wt, x, static_cast<int32_t>(t), static_cast<int32_t>(mode), y, st);
+                    }});
+    return Status::Ok();
+}
+
 Status Builder::argmax(const std::string& name, const float* logits, uint32_t rows, uint32_t v, const uint32_t* ids,
                        uint32_t* tok) {
     ops_.push_back({name, [=](cudaStream_t st) {

@@ -115,6 +115,12 @@ public:
     // null (graph.rs:216-222, quant.wgsl).
     Status quant(const std::string& name, uint32_t k, double eps, const float* x, const float* norm, uint32_t rows,
                  int act, int8_t* xq, float* xs);
+    // The norm_quant prologue and the projection in one launch (graph.rs:266,323 then
+    // 190-198): x f32 [t, k] RMSNorm'ed with `norm` (f32 [k], or none if null),
+    // quantized per token and y (+)= W x, bit-identical to quant + gemv
+    // (w4a8_gemv_x / w4a8_gemv_xn); group-128 weights, t <= 2 with a norm.
+    Status quant_gemv(const std::string& name, const std::string& w, uint32_t k, uint32_t n, uint32_t mode,
+                      uint32_t t, const float* x, const float* norm, double eps, float* y);
     // Greedy token per row of logits [rows, v] (argmax.wgsl, graph.rs:484).
     Status argmax(const std::string& name, const float* logits, uint32_t rows, uint32_t v, const uint32_t* ids,
                   uint32_t* tok);
