@@ -243,6 +243,24 @@ W4A8_API w4a8_status w4a8_lmhead_argmax_xchg(const w4a8_weight* w, int32_t row_o
                                             void* workspace, size_t workspace_bytes, w4a8_xchg* x,
                                             void* stream);
 
+/* MTP speculative step, around the W4A8 path (survey (f): the verify integration).
+ * w4a8_gather_rows (gather_rows.wgsl:1-24, graph.rs:471-516): the one-time gather of
+ * the draft lm_head, row r of (dst_q, dst_s) = row ids[r] of src's packed weights
+ * and scales (dst_q u32[rows, k/8] 16-byte aligned, dst_s in src's scale format);
+ * rows whose id is >= src->n are left untouched.  The draft argmax is then
+ * w4a8_lmhead_argmax on w4a8_weight_view(dst_q, dst_s, rows, ...) with ids mapping
+ * the index back to the vocabulary (argmax.wgsl:41). */
+W4A8_API w4a8_status w4a8_gather_rows(const w4a8_weight* src, const uint32_t* ids, int32_t rows, void* dst_q,
+                                     void* dst_s, void* stream);
+/* w4a8_spec_accept (spec_accept.wgsl:1-38): the end of a step that ran the model on
+ * tok = [x, d] (u32[2], rewritten), with greedy tokens y[2] and MTP drafts e[2]:
+ * a = (d == y[0]); tok = [y[a], e[a]]; ctl = (pos + 1 + a, pos + 3 + a, 2,
+ * (slot + 1 + a) % 3) from params = (pos, seq_len, m, slot) (u32[4]; may be the
+ * previous step's ctl); out (u32[5] or NULL) = (1 + a, y[0], y[1], pos', slot').
+ * All device pointers; one thread. */
+W4A8_API w4a8_status w4a8_spec_accept(uint32_t* tok, const uint32_t* y, const uint32_t* e, const uint32_t* params,
+                                     uint32_t* ctl, uint32_t* out, void* stream);
+
 /* Index carried by a packed argmax key (0 for the "no value > -3e38" key 0). */
 static inline uint32_t w4a8_key_index(uint64_t key) {
     return key ? ~(uint32_t)(key & 0xffffffffu) : 0u;

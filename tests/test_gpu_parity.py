@@ -428,6 +428,54 @@ def test_gemv_norm_quant_fused(cuda, n, k, m, mode, has_min):
             ops.gemv_xn(w, to_dev(make_x(4, k), cuda), to_dev(nw, cuda), eps)
 
 
+@pytest.mark.parametrize("group,has_min", [(32, True), (128, False)])
+def test_gather_rows_and_draft_argmax(cuda, group, has_min):
+    """MTP draft head: rows mtp.head_ids of the (tied) embedding gathered on the GPU
+    equal the oracle's, and the lm_head argmax over them with the ids mapping gives
+    the vocabulary token of the oracle's argmax over those rows."""
+    from oracle import spec
+
+    v, k, rows = 3000, 1024, 517
+    q, s, _ = make_weight(v, k, group, has_min, seed=31)
+    ids = np.random.default_rng(3).choice(v, size=rows, replace=False).astype(np.uint32)
+    w = dev_weight(q, s, v, k, group, has_min, cuda)
+    dids = torch.from_numpy(ids.view(np.int32)).to(cuda)
+    dw = ops.gather_rows(w, dids)
+    gq, gs = spec.gather_rows(q, s, ids)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(dw.q.cpu().numpy().view(np.uint32), gq.view(np.uint32))
+    np.testing.assert_array_equal(dw.s.cpu().numpy().view(gs.dtype), gs)
+    if group == 128:
+        m = 2
+        xq, xs = orc.quant(make_x(m, k, seed=32), act=1)
+        logits = orc.gemv(gq, gs, k, 128, has_min, xq, xs, act=1)
+        want = ids[orc.argmax(logits)]
+        _, tok = ops.lmhead_argmax(dw, to_dev(xq, cuda), to_dev(xs, cuda), act=1, ids=dids)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(tok.cpu().numpy().astype(np.uint32), want)
+
+
+def test_spec_accept_chain(cuda):
+    """Two speculative steps on the GPU (accepted, then rejected), the second reading
+    the first's ctl as its params, against the oracle."""
+    from oracle import spec
+
+    def i32(a):
+        return torch.tensor(np.asarray(a, dtype=np.uint32).view(np.int32), device=cuda)
+
+    tok, params = [5, 9], (100, 102, 2, 1)
+    steps = [([9, 11], [21, 22]), ([3, 4], [7, 8])]  # y[0] == d accepts; then tok[1] = 22 != 3 rejects
+    dtok, dctl, dout = i32(tok), i32(params), i32([0] * 5)
+    for y, e in steps:
+        want_tok, want_ctl, want_out = spec.spec_accept(tok, y, e, params)
+        ops.spec_accept(dtok, i32(y), i32(e), dctl, dctl, dout)  # params alias ctl
+        torch.cuda.synchronize()
+        assert dtok.cpu().numpy().view(np.uint32).tolist() == want_tok.tolist()
+        assert dctl.cpu().numpy().view(np.uint32).tolist() == want_ctl.tolist()
+        assert dout.cpu().numpy().view(np.uint32).tolist() == want_out.tolist()
+        tok, params = want_tok.tolist(), tuple(want_ctl.tolist())
+
+
 def test_gemv_fused_quant_rejects_group32(cuda):
     q, s, _ = make_weight(32, 256, 32, True, seed=1)
     w = dev_weight(q, s, 32, 256, 32, True, cuda)

@@ -227,6 +227,27 @@ def lmhead_argmax_sharded(w, xq, xs, row_offset, act=ACT_TOKEN, group=None, ids=
     return best_key, keys_to_tokens(best_key, ids)
 
 
+def gather_rows(w, ids):
+    """The draft lm_head of an MTP step: rows ids (int32/uint32 [rows] on the device)
+    of w's packed weights and scales, as a new QWeight (gather_rows.wgsl)."""
+    _need_cuda(ids)
+    rows = ids.numel()
+    q = torch.empty((rows, w.k // 8), dtype=torch.int32, device=ids.device)
+    sdt = torch.int32 if w.has_min else torch.int16
+    s = torch.empty((rows, w.k // w.group), dtype=sdt, device=ids.device)
+    _lib.check(_lib.load().w4a8_gather_rows(ctypes.byref(w.c), _ptr(ids), rows, _ptr(q), _ptr(s), _stream()))
+    return QWeight(q, s, rows, w.k, w.group, w.has_min)
+
+
+def spec_accept(tok, y, e, params, ctl, out=None):
+    """End of a speculative step (spec_accept.wgsl), all int32 device tensors: tok [2]
+    (rewritten), y [2], e [2], params [4] -> ctl [4] (may be params), out [5] or None."""
+    _need_cuda(tok, y, e, params, ctl, out)
+    _lib.check(_lib.load().w4a8_spec_accept(_ptr(tok), _ptr(y), _ptr(e), _ptr(params), _ptr(ctl), _ptr(out),
+                                            _stream()))
+    return tok, ctl, out
+
+
 XCHG_HANDLE_BYTES = 64
 
 
