@@ -20,24 +20,24 @@
 //    SM path can sustain at tensor-core speed.
 //  - Weight rows are the MMA M (one TMEM lane per row), tokens the MMA N: the
 //    per-group scale s[n, g] is a per-lane constant in the epilogue.
-//  - The packed weights go straight from global memory into registers of the
-//    expansion warps (two groups ahead, so their latency is hidden), which write
-//    16*(q-8) per byte into the K-major 128-byte-swizzled A tile: the nibble q^8
-//    (the 4-bit two's complement of q-8) lands in the high half of the byte, so
-//    its sign extends for free; the factor 16 is folded into the scale (exact).
-//    No shared-memory copy of the packed weights is made: shared-memory bandwidth
-//    is the other limit of this kernel.
+//  - The packed weights arrive by TMA (a 3-D map of 4 groups x 128 rows x 64 B with
+//    64-byte swizzle, so the row reads are conflict-free).  The epilogue warps
+//    expand each group kLead groups ahead of its MMA into an int8 weight tile in
+//    TMEM (the MMA's A operand): 16*(q-8) per byte, the nibble q^8 (the 4-bit
+//    two's complement of q-8) in the high half of the byte, so its sign extends
+//    for free; the factor 16 is folded into the scale (exact).  Keeping A in TMEM
+//    spares shared-memory bandwidth, the other limit of this kernel.
 //  - Activations come by TMA, four groups (4 x 8 KB) per copy through a 3-D
 //    tensor map (k-inner 128 bytes, tokens, groups), so every group lands as its
-//    own swizzled K-major block.
+//    own swizzled K-major block (the MMA's B operand).
 //  - Each TMEM accumulator is pre-set to the bits of 1.5*2^23 and the MMA adds the
 //    group's dots onto it (|16 I| < 2^22), so the accumulator read back as a float
 //    is exactly 1.5*2^23 + 16 I; one packed subtract and one packed FMA per two
 //    values finish the scale step, and writing the bias back re-arms the buffer.
-//    Four TMEM buffers of 128 columns (all 512) let the tensor core run four
-//    groups ahead of the epilogue.
+//    Three accumulator buffers of 128 columns and four int8 weight tiles of 32
+//    columns fill TMEM's 512 columns.
 //
-// Warp roles per CTA (10 warps, 200 registers each): 0 weight and activation TMA,
+// Warp roles per CTA (10 warps, 168 registers each): 0 weight and activation TMA,
 // 1 MMA issue (cluster rank 0 only; a tcgen05.mma blocks its thread for about its
 // own duration) and TMEM allocation, 2-9 epilogue: int4 -> int8 expansion kLead
 // groups ahead and the scale step (two halves of 64 columns; warp % 4 is the TMEM
@@ -77,7 +77,7 @@ constexpr uint32_t kTmemA = kDBufs * kTok;  // first column of the weight tiles
 static_assert(kTmemA + kABufs * 32 <= kTmemCols, "TMEM plan exceeds 512 columns");
 static_assert(kLead < kABufs && kLead < kDBufs + 1, "expansion lead exceeds the buffers");
 constexpr int kEpiWarp0 = 2, kEpiWarps = 8;
-constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 320: 200 registers per thread
+constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 320 (allocated as 384: 168 registers a thread)
 constexpr uint32_t kBias = 0x4B400000u;                  // bits of 1.5 * 2^23
 constexpr float kBiasF = 12582912.0f;
 
