@@ -4,7 +4,9 @@ the vocabulary rows and the keys are exchanged (a) through torch.distributed NCC
 over its own NCCL communicator) and (c) over peer memory (w4a8_lmhead_argmax_xchg:
 three calls, so both halves of the double-buffered key slots are used, then two
 replays of a captured CUDA graph).  All must give the one-device argmax of the
-oracle bit for bit, on every rank.  Skipped with fewer than 2 GPUs."""
+oracle bit for bit, on every rank.  Then rank 0 makes a call rank 1 never joins:
+its bounded wait must give up with ETIMEOUT and its own key, and the context must
+stay usable.  Skipped with fewer than 2 GPUs."""
 
 import datetime
 import os
@@ -48,6 +50,7 @@ def _rank(rank, world, port, results):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
     from webyiq_b200 import ops
+    from webyiq_b200._lib import ETIMEOUT, W4A8Error
 
     q, s, xq, xs = _data()
     per = V // world
@@ -92,9 +95,26 @@ def _rank(rank, world, port, results):
         got3.append((key3.tolist(), tok3.tolist()))
     err = ops.device_error()
     del g
+    dist.barrier()
+    # failure detection: rank 0 makes one more call that rank 1 never joins; its
+    # bounded flag wait gives up, it keeps its own shard's key and the context
+    # stays usable
+    timeout_seen = None
+    if rank == 0:
+        key3.zero_()
+        ops.lmhead_argmax_xchg(w, xq_d, xs_d, xchg, act=ops.ACT_TOKEN, row_offset=lo, workspace=ws, best_key=key3,
+                               tok=tok3)
+        try:
+            ops.device_error()
+            timeout_seen = False
+        except W4A8Error as exc:
+            timeout_seen = exc.status == ETIMEOUT
+        own = ops.lmhead_argmax(w, xq_d, xs_d, act=ops.ACT_TOKEN, row_offset=lo, workspace=ws)[0]
+        torch.cuda.synchronize()
+        timeout_seen = timeout_seen and key3.tolist() == own.tolist()
     dist.barrier()  # no rank closes its buffer while a peer may still store into it
     xchg.close()
-    results[rank] = (key1.tolist(), tok1.tolist(), key2.tolist(), tok2.tolist(), got3, err)
+    results[rank] = (key1.tolist(), tok1.tolist(), key2.tolist(), tok2.tolist(), got3, err, timeout_seen)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -112,9 +132,10 @@ def test_lmhead_split_two_gpus(cuda):
     ref_tok = orc.argmax(logits).astype(np.int64).tolist()
     ref_key = [to_i64(shard_key(row, 0)) for row in logits]
     for r in range(world):
-        key1, tok1, key2, tok2, got3, err = got[r]
+        key1, tok1, key2, tok2, got3, err, timeout_seen = got[r]
         assert key1 == ref_key and key2 == ref_key, r
         assert tok1 == ref_tok and tok2 == ref_tok, r
         assert err == 0, r
         for i, (key3, tok3) in enumerate(got3):
             assert key3 == ref_key and tok3 == ref_tok, (r, i)
+    assert got[0][6] is True  # the unmatched call timed out, kept its own key, context usable
