@@ -7,13 +7,15 @@ larger than the 126 MB L2), run back to back as one decode step's matvec sequenc
 Weights: signed int4 uniform in [-8, 7] (uniform random nibbles), group 128, fp16
 scales |N(0,1)|*0.01; activations fp32 N(0,1) quantized per token to int8.
 
-  value   algorithmic GB/s of the step (SURVEY 8d byte formula), inputs resident in
-          HBM, the 144 GEMV launches replayed as one CUDA graph with programmatic
-          dependent launch between them;
-  e2e     the same metric through the public API with host buffers: per step one
-          pinned-host -> device copy of the 144 fp32 input vectors, 144 launches of
-          the GEMV with the per-token quant fused in (w4a8_gemv_x), one device ->
-          host copy of all outputs;
+  value   algorithmic GB/s of the step (packed weights + scales + activations +
+          outputs per projection), inputs resident in HBM, the 144 GEMV launches
+          replayed as one CUDA graph with programmatic dependent launch between
+          them;
+  e2e     the same metric through the public API with host buffers: per step the
+          pinned-host -> device copies of the 144 fp32 input vectors, 144 launches
+          of the GEMV with the per-token quant fused in (w4a8_gemv_x), and the
+          device -> host copies of all outputs; the copies of later layers' inputs
+          and earlier layers' outputs overlap the chain on a side stream;
   extra   secondary BASELINE metrics from the same run: config 1 (single GEMV),
           config 3 (lm_head + fused argmax, tok/s), config 4 (prefill GEMM, TOPS),
           config 5 (batched GEMV, M = 2..16).
@@ -180,6 +182,7 @@ class Sweep:
         self.h_out = torch.empty(self.nout).pin_memory()
         self.d_in = torch.empty(self.nin, device=dev)
         self.d_out = torch.empty(self.nout, device=dev)
+        self.side = torch.cuda.Stream(device=dev)  # e2e: copies that overlap the GEMV chain
 
     def step(self):
         ops = self.ops
@@ -189,16 +192,38 @@ class Sweep:
                 ops.gemv(w, xq, xs, act=ops.ACT_TOKEN, y=self.y[(k, n)])
 
     def step_e2e(self):
-        ops = self.ops
-        self.d_in.copy_(self.h_in, non_blocking=True)
+        """One step from pinned host buffers: every input goes up and every output comes
+        down inside the step.  The inputs of layers 0-1 are copied first; the other
+        layers' inputs go up on a side stream while those two run, and the outputs of
+        all but the last two layers come down on the side stream while those two run.
+        The GEMV chain waits for the side stream once: a kernel that waits on another
+        stream starts only when its predecessor has finished (no early launch), which
+        costs about 6 us per wait."""
+        torch, ops = self.torch, self.ops
+        main, side = torch.cuda.current_stream(), self.side
+        fin, fout = sum(k for k, _ in SWEEP), sum(n for _, n in SWEEP)  # floats per layer
+        self.d_in[:2 * fin].copy_(self.h_in[:2 * fin], non_blocking=True)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            self.d_in[2 * fin:].copy_(self.h_in[2 * fin:], non_blocking=True)
+            up_rest = torch.cuda.Event()
+            up_rest.record(side)
+        tail = LAYERS - 2  # first layer whose outputs the main stream copies down
         i = o = 0
-        for layer in self.w:
+        for li, layer in enumerate(self.w):
+            if li == 2:
+                main.wait_event(up_rest)
+            elif li == tail:
+                side.wait_stream(main)
+                with torch.cuda.stream(side):
+                    self.h_out[:tail * fout].copy_(self.d_out[:tail * fout], non_blocking=True)
             for (k, n), w in zip(SWEEP, layer):
                 x = self.d_in[i:i + k].view(1, k)
                 # per-token quant fused into the GEMV launch (w4a8_gemv_x)
                 ops.gemv_x(w, x, y=self.d_out[o:o + n].view(1, n))
                 i, o = i + k, o + n
-        self.h_out.copy_(self.d_out, non_blocking=True)
+        self.h_out[tail * fout:].copy_(self.d_out[tail * fout:], non_blocking=True)
+        main.wait_stream(side)
 
     launches_per_step = LAYERS * len(SWEEP)
 
@@ -551,7 +576,8 @@ def main():
     try:
         ms_e2e, g2 = time_graph(torch, sweep.step_e2e, args.steps, args.warmup, sync_all)
         del g2
-        e2e_mode = "cuda graph of H2D copy + fused quant/GEMV (w4a8_gemv_x) + D2H copy"
+        e2e_mode = ("cuda graph: H2D copies of all inputs + fused quant/GEMV (w4a8_gemv_x) + D2H copies of all "
+                    "outputs, the copies of layers 2-23 (up) and 0-21 (down) overlapping the chain on a side stream")
     except Exception as exc:  # capture of the host copies unsupported: time eagerly
         e2e_mode = f"eager ({type(exc).__name__})"
         for _ in range(args.warmup):
@@ -565,6 +591,9 @@ def main():
         e1.record()
         torch.cuda.synchronize()
         ms_e2e = e0.elapsed_time(e1) / args.steps
+    torch.cuda.synchronize()
+    if not (torch.equal(sweep.d_in.cpu(), sweep.h_in) and torch.equal(sweep.d_out.cpu(), sweep.h_out)):
+        raise RuntimeError("e2e: the host and device copies of the step's inputs or outputs differ")
     if dist is not None:
         t = torch.tensor([ms_e2e], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -223,8 +223,8 @@ W4A8_API w4a8_status w4a8_nccl_comm_destroy(void* comm);
  * device, so the calls can be captured in a CUDA graph; every rank must make the
  * same number of calls with the same m (<= W4A8_XCHG_MAX_TOKENS).  A wait that
  * gives up leaves this rank's own keys in best_key and sets the device error word
- * (w4a8_device_error reports W4A8_ETIMEOUT).  No counterpart in the reference (the
- * exchange step of its sharded head, survey row (e), done over peer memory). */
+ * (w4a8_device_error reports W4A8_ETIMEOUT).  No counterpart in the reference: this is
+ * the exchange step of a column-split head, done over peer memory. */
 #define W4A8_XCHG_HANDLE_BYTES 64
 #define W4A8_XCHG_MAX_RANKS 8
 #define W4A8_XCHG_MAX_TOKENS 16
@@ -243,7 +243,7 @@ W4A8_API w4a8_status w4a8_lmhead_argmax_xchg(const w4a8_weight* w, int32_t row_o
                                             void* workspace, size_t workspace_bytes, w4a8_xchg* x,
                                             void* stream);
 
-/* MTP speculative step, around the W4A8 path (survey (f): the verify integration).
+/* MTP speculative step, around the W4A8 path (the verify integration).
  * w4a8_gather_rows (gather_rows.wgsl:1-24, graph.rs:471-516): the one-time gather of
  * the draft lm_head, row r of (dst_q, dst_s) = row ids[r] of src's packed weights
  * and scales (dst_q u32[rows, k/8] 16-byte aligned, dst_s in src's scale format);

@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this directory from the reference's own Python.
 
-Run in a container that has the reference checkout (default /root/reference, or
-the REFERENCE env var); the GPU box and the test suite only read the .npz files.
+Run where the reference checkout is present, with its root in the REFERENCE
+environment variable; the GPU box and the test suite only read the .npz files.
 
   convert_q4.npz     tools/convert.py quantize_q4 (group 32, with and without the
                      clip search; group 128) and pack_q4 on the symmetric signed
@@ -10,7 +10,7 @@ the REFERENCE env var); the GPU box and the test suite only read the .npz files.
                      hook, executed from the reference source) and its fake-quant
                      linear: F.linear(fq_input(x), quantize_q4(W, 32)[2]) in fp32
 
-    python tests/golden/make_golden.py
+    REFERENCE=<reference checkout> python tests/golden/make_golden.py
 """
 
 import ast
@@ -20,7 +20,7 @@ import sys
 import numpy as np
 import torch
 
-REF = os.environ.get("REFERENCE", "/root/reference")
+REF = os.environ.get("REFERENCE", "")
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
@@ -39,6 +39,8 @@ def reference_fq_input():
 
 
 def main():
+    if not REF or not os.path.isfile(os.path.join(REF, "tools", "convert.py")):
+        sys.exit("set REFERENCE to the reference checkout (the directory holding tools/convert.py)")
     sys.path.insert(0, os.path.join(REF, "tools"))
     import convert  # the reference's converter
 
