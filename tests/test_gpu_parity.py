@@ -354,12 +354,14 @@ def test_gemv_fused_quant_bit_exact(cuda, has_min, nk, m, mode):
 @pytest.mark.parametrize("mode", [0, 1, 2])
 @pytest.mark.parametrize("m", [1, 2])
 @pytest.mark.parametrize("n,k", [(6144, 2048), (2048, 6144), (2048, 4096), (512, 2048), (14000, 2048),
-                                 (3000, 1024), (600, 384), (1500, 2560), (20000, 2048)])
+                                 (3000, 1024), (600, 384), (1500, 2560), (4096, 6144), (20000, 2048)])
 def test_gemv_decode_shapes(cuda, n, k, m, mode, has_min, fq):
     """The decode GEMV (one or two tokens into y) over each split of a row between
     lanes (8, 16 or 32 lanes of one or two groups, idle lanes past the row's end),
-    one to four row passes per CTA, a zero activation row, and (20000, 2048), which
-    exceeds its shared-memory plan and takes the tensor-core GEMV.  Bit-exact with
+    one to four row passes per CTA, a zero activation row, both CTA configurations
+    (three per SM where the rows fit, else two: (14000, 2048) and (4096, 6144) at one
+    token), and (20000, 2048), which exceeds its shared-memory plan and takes the
+    tensor-core GEMV.  Bit-exact with
     the oracle (SWIGLU within 1e-3: expf) and with the dp4a GEMV, fused quant or not."""
     q, s, _ = make_weight(n, k, 128, has_min, seed=n + k + m + mode)
     x = make_x(m, k, seed=k + m)

@@ -45,12 +45,19 @@ namespace {
 
 constexpr int kDecMaxPass = 4;                 // row passes per CTA (scale registers)
 constexpr int kDecVPT = 8;                     // fused quant: float4s of x per thread (per token)
-constexpr size_t kDecSmemBudget = 100 * 1024;  // two CTAs per SM
 
-template <int MT, int GPL>
-struct DecThreads {
-    static constexpr int value = MT * GPL == 1 ? 384 : 256;  // two CTAs' registers fit an SM
+// CTAs per SM.  DEEP (one token, when its rows fit 72 KB): three CTAs, so the CTAs
+// of the next two calls are resident and copying their weights while this one
+// computes; 256 threads with one group per lane (K <= 4096), 128 with two (~130
+// registers).  Otherwise two CTAs: 384 threads for one token and one group per
+// lane, which covers more rows per CTA, 256 for the rest.
+template <int MT, int GPL, bool DEEP>
+struct DecCfg {
+    static constexpr int threads = DEEP ? (MT * GPL == 1 ? 256 : 128) : (MT * GPL == 1 ? 384 : 256);
+    static constexpr int blocks = DEEP ? 3 : 2;  // registers: 3 x 256 x 80 or 3 x 128 x 130; 2 x 384 x 80
 };
+constexpr size_t kDecSmemDeep = 72 * 1024;     // three CTAs per SM
+constexpr size_t kDecSmemBudget = 100 * 1024;  // two CTAs per SM
 
 struct DecParams {
     const unsigned char* q;  // [rows][k/2]
@@ -73,12 +80,12 @@ __device__ __forceinline__ int pack_fix(uint32_t h) {
     return (f.mant << 8) | f.sh;
 }
 
-template <bool HAS_MIN, int MODE, int MT, int GPL, bool FQ, bool NORM>
-__global__ void __launch_bounds__(DecThreads<MT, GPL>::value, 2) gemv_dec_kernel(const DecParams p) {
+template <bool HAS_MIN, int MODE, int MT, int GPL, bool FQ, bool NORM, bool DEEP>
+__global__ void __launch_bounds__(DecCfg<MT, GPL, DEEP>::threads, DecCfg<MT, GPL, DEEP>::blocks) gemv_dec_kernel(const DecParams p) {
     constexpr bool SWI = MODE == W4A8_SWIGLU;
     constexpr int NH = SWI ? 2 : 1;  // weight rows per output row (gate, up)
     constexpr int kSteps = 4 * GPL;  // 16-byte chunks per lane per row
-    constexpr int T = DecThreads<MT, GPL>::value;
+    constexpr int T = DecCfg<MT, GPL, DEEP>::threads;
     constexpr int NW = T / 32;
     extern __shared__ __align__(128) unsigned char smem[];
 
@@ -399,16 +406,16 @@ DecShape dec_shape(int kg, int m) {
 
 struct DecPlan {
     DecShape sh;
+    bool deep;  // three CTAs per SM
     int ctas, rows_max, threads;
     int sc_off, sc_half;
     size_t smem;
 };
 
-bool dec_plan(const GemvParams& g, bool has_min, int mode, DecPlan& pl) {
-    if (g.m < 1 || g.m > 2 || g.k % 128 != 0 || g.n_out < 1) return false;
-    pl.sh = dec_shape(g.k / 128, g.m);
-    if (pl.sh.L == 0) return false;
-    pl.threads = g.m * pl.sh.gpl == 1 ? 384 : 256;
+// The plan for CTAs of `threads` threads; whether it fits `budget` bytes of shared
+// memory, kDecMaxPass row passes and the fused quant's registers.
+bool dec_fit(const GemvParams& g, bool has_min, int mode, int threads, size_t budget, DecPlan& pl) {
+    pl.threads = threads;
     const int sms = sm_count();
     pl.ctas = g.n_out < sms ? g.n_out : sms;
     pl.rows_max = (g.n_out + pl.ctas - 1) / pl.ctas;
@@ -422,27 +429,45 @@ bool dec_plan(const GemvParams& g, bool has_min, int mode, DecPlan& pl) {
     const int npass = (pl.rows_max + rows_per_pass - 1) / rows_per_pass;
     const int xs = g.norm_w ? 256 : pl.threads;  // the threads that hold x (the norm's partition)
     const bool vpt_ok = !g.xf32 || (g.k / 4 + xs - 1) / xs <= (g.m == 1 ? kDecVPT : kDecVPT / 2);
-    return pl.smem <= kDecSmemBudget && npass <= kDecMaxPass && vpt_ok;
+    return pl.smem <= budget && npass <= kDecMaxPass && vpt_ok;
 }
 
-template <bool HAS_MIN, int MODE, int MT, int GPL, bool FQ, bool NORM>
+bool dec_plan(const GemvParams& g, bool has_min, int mode, DecPlan& pl) {
+    if (g.m < 1 || g.m > 2 || g.k % 128 != 0 || g.n_out < 1) return false;
+    pl.sh = dec_shape(g.k / 128, g.m);
+    if (pl.sh.L == 0) return false;
+    const bool one = g.m * pl.sh.gpl == 1;
+    // three CTAs per SM for one token (with two groups a lane: 128 threads, and not
+    // with the norm, whose partition of x needs 256)
+    pl.deep = g.m == 1 && (one || !g.norm_w) &&
+              dec_fit(g, has_min, mode, one ? DecCfg<1, 1, true>::threads : DecCfg<1, 2, true>::threads, kDecSmemDeep, pl);
+    if (pl.deep) return true;
+    return dec_fit(g, has_min, mode, one ? DecCfg<1, 1, false>::threads : DecCfg<2, 1, false>::threads, kDecSmemBudget, pl);
+}
+
+template <bool HAS_MIN, int MODE, int MT, int GPL, bool FQ, bool NORM, bool DEEP>
 w4a8_status dec_inst(const DecParams& p, const DecPlan& pl, cudaStream_t st) {
     static size_t configured = 0;  // set on first use: static shared memory counts against the default 48 KB too
-    auto kernel = gemv_dec_kernel<HAS_MIN, MODE, MT, GPL, FQ, NORM>;
+    auto kernel = gemv_dec_kernel<HAS_MIN, MODE, MT, GPL, FQ, NORM, DEEP>;
     if (pl.smem > configured) {
         const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pl.smem));
         if (e != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8 gemv (decode): smem attribute: %s", cudaGetErrorString(e));
+        const cudaError_t c = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (c != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8 gemv (decode): carveout: %s", cudaGetErrorString(c));
         configured = pl.smem;
     }
-    return launch_pdl("w4a8 gemv (decode)", kernel, dim3(pl.ctas), dim3(DecThreads<MT, GPL>::value), pl.smem, st, p);
+    return launch_pdl("w4a8 gemv (decode)", kernel, dim3(pl.ctas), dim3(DecCfg<MT, GPL, DEEP>::threads), pl.smem, st, p);
 }
 
 template <bool HAS_MIN, int MODE, bool FQ, bool NORM>
 w4a8_status dec_shape_dispatch(const DecParams& p, const DecPlan& pl, cudaStream_t st) {
+    if (p.m == 1 && pl.sh.gpl == 1)
+        return pl.deep ? dec_inst<HAS_MIN, MODE, 1, 1, FQ, NORM, true>(p, pl, st)
+                       : dec_inst<HAS_MIN, MODE, 1, 1, FQ, NORM, false>(p, pl, st);
     if (p.m == 1)
-        return pl.sh.gpl == 1 ? dec_inst<HAS_MIN, MODE, 1, 1, FQ, NORM>(p, pl, st)
-                              : dec_inst<HAS_MIN, MODE, 1, 2, FQ, NORM>(p, pl, st);
-    return dec_inst<HAS_MIN, MODE, 2, 1, FQ, NORM>(p, pl, st);
+        return pl.deep && !NORM ? dec_inst<HAS_MIN, MODE, 1, 2, FQ, false, true>(p, pl, st)
+                                : dec_inst<HAS_MIN, MODE, 1, 2, FQ, NORM, false>(p, pl, st);
+    return dec_inst<HAS_MIN, MODE, 2, 1, FQ, NORM, false>(p, pl, st);
 }
 
 template <bool HAS_MIN, bool FQ, bool NORM = false>
