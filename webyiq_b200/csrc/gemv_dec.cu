@@ -44,7 +44,9 @@ int sm_count();  // capi.cu
 namespace {
 
 constexpr int kDecMaxPass = 4;                 // row passes per CTA (scale registers)
-constexpr int kDecVPT = 8;                     // fused quant: float4s of x per thread (per token)
+// fused quant: float4s of x a thread holds per token (12 in the 128-thread CTAs,
+// so that K = 6144 fits them)
+constexpr int dec_vpt(int m, int threads) { return m == 1 ? (threads <= 128 ? 12 : 8) : 4; }
 
 // CTAs per SM.  DEEP (one token, when its rows fit 72 KB): three CTAs, so the CTAs
 // of the next two calls are resident and copying their weights while this one
@@ -195,7 +197,7 @@ __global__ void __launch_bounds__(DecCfg<MT, GPL, DEEP>::threads, DecCfg<MT, GPL
         // row), rint(x * inv).  One pass over x: each thread keeps its float4s in
         // registers across the amax exchange.  A warp's 32 neighbouring float4s are
         // one 128-group, so the group sums come from warp shuffles.
-        constexpr int VPT = MT == 1 ? kDecVPT : kDecVPT / 2;
+        constexpr int VPT = dec_vpt(MT, T);
         // With the norm, the first 256 threads hold x as the quant kernel's 256
         // threads do (float4 t + 256 j), so the sum of squares is added in the same
         // order and the RMS scale has the same bits.
@@ -428,7 +430,7 @@ bool dec_fit(const GemvParams& g, bool has_min, int mode, int threads, size_t bu
     const int rows_per_pass = (pl.threads / 32) * (32 / pl.sh.L);
     const int npass = (pl.rows_max + rows_per_pass - 1) / rows_per_pass;
     const int xs = g.norm_w ? 256 : pl.threads;  // the threads that hold x (the norm's partition)
-    const bool vpt_ok = !g.xf32 || (g.k / 4 + xs - 1) / xs <= (g.m == 1 ? kDecVPT : kDecVPT / 2);
+    const bool vpt_ok = !g.xf32 || (g.k / 4 + xs - 1) / xs <= dec_vpt(g.m, threads);
     return pl.smem <= budget && npass <= kDecMaxPass && vpt_ok;
 }
 
