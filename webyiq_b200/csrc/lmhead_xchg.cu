@@ -9,7 +9,7 @@
 // Against the NCCL all-reduce of lmhead_multi.cu this replaces a collective launch
 // and a key-to-token kernel by one kernel that starts under programmatic dependent
 // launch while the lm_head kernel finishes; the exchange itself is one store per
-// (peer, token) and one flag per peer.
+// (peer, token) and one flag per peer, each peer served by its own thread.
 //  - Key slots are double-buffered by the parity of the call's sequence number: a
 //    rank that runs ahead writes its next keys into the other half, and it cannot
 //    run two calls ahead, since each call waits for every rank's flag.
@@ -65,29 +65,31 @@ __global__ void __launch_bounds__(32) lmhead_xchg_kernel(const XchgPeers peers, 
     __shared__ unsigned int s_seq;
     __shared__ int s_ok;
     const int tid = threadIdx.x;
-    if (tid == 0) s_seq = *reinterpret_cast<volatile unsigned int*>(&me->seq) + 1u;
-    __syncthreads();
-    const unsigned int seq = s_seq, par = seq & 1u;
     if (tid == 0) {
-        // this rank's keys into slot [par][rank] of every rank, each peer's keys
-        // published by a release store of the flag (it orders this thread's stores)
-        for (int r = 0; r < world; ++r) {
-            for (int t = 0; t < m; ++t) st_relaxed_sys(&peers.buf[r]->key[par][rank][t], best_key[t]);
-            st_release_sys(&peers.buf[r]->flag[rank], seq);
-        }
-        bool ok = true;
-        const long long t0 = clock64();
-        for (int r = 0; r < world && ok; ++r)
-            while (static_cast<int>(ld_acquire_sys(&me->flag[r]) - seq) < 0)
-                if (clock64() - t0 > static_cast<long long>(kWaitLimitCycles)) {
-                    ok = false;
-                    break;
-                }
-        if (!ok) atomicOr(err, DEV_ERR_XCHG_TIMEOUT);
-        me->seq = seq;  // the calls stay counted alike on every rank
-        s_ok = ok;
+        s_seq = *reinterpret_cast<volatile unsigned int*>(&me->seq) + 1u;
+        s_ok = 1;
     }
     __syncthreads();
+    const unsigned int seq = s_seq, par = seq & 1u;
+    if (tid < world) {
+        // Thread r serves peer r: this rank's keys into slot [par][rank] of rank r's
+        // buffer, published by a release store of the flag (it orders this thread's
+        // stores).  One thread per peer, so the system-scope releases run side by
+        // side instead of one after another.
+        const int r = tid;
+        for (int t = 0; t < m; ++t) st_relaxed_sys(&peers.buf[r]->key[par][rank][t], best_key[t]);
+        st_release_sys(&peers.buf[r]->flag[rank], seq);
+        // then the same thread waits (bounded) for rank r's flag in this buffer
+        const long long t0 = clock64();
+        while (static_cast<int>(ld_acquire_sys(&me->flag[r]) - seq) < 0)
+            if (clock64() - t0 > static_cast<long long>(kWaitLimitCycles)) {
+                s_ok = 0;
+                atomicOr(err, DEV_ERR_XCHG_TIMEOUT);
+                break;
+            }
+    }
+    __syncthreads();  // every flag acquired (or given up) before the keys are read
+    if (tid == 0) me->seq = seq;  // the calls stay counted alike on every rank
     if (tid < m) {
         unsigned long long k = best_key[tid];
         if (s_ok) {
