@@ -22,7 +22,8 @@ scales |N(0,1)|*0.01; activations fp32 N(0,1) quantized per token to int8.
 
 --impl reference times the reference's CPU path (tools/reference.py: int4 weights
 dequantized once, int8 activation fake-quant + fp32 F.linear per projection) on
-the host cores, for the same metric and config.
+the host cores, for the same metric and config; its `extra` holds config 3 (the
+lm_head over the 248,320-token vocabulary plus argmax) through the same path.
 
 Multi-GPU (torchrun, one rank per GPU): the decode sweep runs as independent
 replicas (weak scaling, no collective); value = all ranks' bytes / max-over-ranks
@@ -446,7 +447,43 @@ def reference_arm(args, rank, world):
                          "sample": f"one layer (6 projections) x {reps} per step, median of {args.steps} steps; "
                                    "tools/reference.py fake-quant F.linear fp32, weights dequantized once"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "extra": {"c3_lmhead_argmax": cpu_lmhead_argmax(torch, fakequant, cores)},
     }
+
+
+C3_K, C3_VOCAB = 2048, 248320  # config 3: the lm_head of the 248,320-token vocabulary
+
+
+def cpu_lmhead_argmax(torch, fakequant, cores, tokens=3):
+    """Config 3 on the host cores through the reference's CPU path: activation
+    fake-quant, fp32 F.linear against the dequantized vocabulary (dequantized once,
+    in row blocks, outside the timed region), then argmax (lowest index among
+    equal maxima, as the reference's argmax).  Per-token latency, median of
+    `tokens` tokens after one warm-up."""
+    g = torch.Generator().manual_seed(3)
+    k, vocab = C3_K, C3_VOCAB
+    wd = torch.empty((vocab, k))
+    for r0 in range(0, vocab, 16384):
+        r1 = min(vocab, r0 + 16384)
+        codes = torch.randint(-8, 8, (r1 - r0, k), generator=g, dtype=torch.int8).float()
+        sc = (torch.randn((r1 - r0, k // GROUP), generator=g).abs() * 0.01).half().float()
+        wd[r0:r1] = codes * sc.repeat_interleave(GROUP, dim=1)
+    x = torch.randn((1, k), generator=g)
+
+    def one():
+        return int(torch.argmax(fakequant.fake_quant_linear(x, wd, per_token=True)))
+
+    one()
+    times = []
+    for _ in range(tokens):
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+    per = statistics.median(times)
+    del wd
+    return {"us_per_token": round(per * 1e6, 1), "tok_s": round(1.0 / per, 2),
+            "gbs_total": round(gemv_bytes(k, vocab) / per / 1e9, 3), "cores": cores,
+            "sample": f"{tokens} tokens after one warm-up, median; fp32 weights dequantized once"}
 
 
 def cpu_baseline_sample(seconds=10.0):
