@@ -16,6 +16,10 @@
  *    the calling thread.  Shapes, modes and pointer alignment are validated on the
  *    host before any launch, so an EINVAL call launches nothing.
  *  - Calls on distinct streams are thread-safe.
+ *  - One GPU per process: each kernel's shared-memory limit is raised once per
+ *    process, at its first call, on the device current then.  A process that
+ *    drives several GPUs gets W4A8_ECUDA from larger calls on the others.  Run one
+ *    process per GPU, as torch.distributed and NCCL ranks do.
  *
  * Weight layout (tools/convert.py:7-12, 68-75 of the reference): a quantized linear
  * weight with n output rows and k inputs is
