@@ -276,7 +276,17 @@ def run_extras(torch, ops, dev, steps, warmup, world, rank, dist):
     out["c1_gemv"] = {"us": round(per * 1e3, 3), "gbs": round(gemv_bytes(k, n) / (per * 1e-3) / 1e9, 1),
                       "frac_hbm": round(gemv_bytes(k, n) / (per * 1e-3) / 1e9 / hbm, 3)}
     del ws
-    # config 5: batched decode / verify, M in {2, 4, 8, 16}, rotating weights
+    def max_ms(ms):
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sync_all = (lambda: dist.barrier()) if world > 1 else None
+    # config 5: batched decode / verify, M in {2, 4, 8, 16}, rotating weights; at
+    # N > 1 every rank runs its own replica (no collective) and the aggregate is all
+    # ranks' bytes over the max-over-ranks time
     c5 = {}
     for k, n in ((2048, 6144), (6144, 2048)):
         ws = [rand_weight(n, k, GROUP, gen, dev, torch, ops) for _ in range(16)]
@@ -288,12 +298,16 @@ def run_extras(torch, ops, dev, steps, warmup, world, rank, dist):
                 for w in ws:
                     ops.gemv(w, xq, xs, act=ops.ACT_TOKEN, y=y)
 
-            ms, g = time_graph(torch, c5f, max(steps // 2, 3), warmup)
+            ms, g = time_graph(torch, c5f, max(steps // 2, 3), warmup, sync_all)
             del g
-            per = ms / len(ws)
-            c5[f"{k}x{n}_m{m}"] = {"us": round(per * 1e3, 3),
-                                   "gbs": round(gemv_bytes(k, n, m) / (per * 1e-3) / 1e9, 1)}
+            per = max_ms(ms) / len(ws)
+            gbs = gemv_bytes(k, n, m) / (per * 1e-3) / 1e9
+            c5[f"{k}x{n}_m{m}"] = {"us": round(per * 1e3, 3), "gbs_per_gpu": round(gbs, 1),
+                                   "gbs_all_gpus": round(world * gbs, 1),
+                                   "tokens_s_all_gpus": round(world * m / (per * 1e-3), 1)}
         del ws
+    c5["replicas"] = world
+    c5["timing"] = "per GPU: max over ranks of the CUDA-event time; all GPUs: world x bytes (or tokens) / that time"
     out["c5_batched_gemv"] = c5
     # config 3: lm_head + fused argmax, vocab column-split over the ranks
     k, vocab = 2048, 248320
@@ -325,19 +339,13 @@ def run_extras(torch, ops, dev, steps, warmup, world, rank, dist):
         ops.lmhead_argmax_allreduce(w, xq, xs, comm, act=ops.ACT_TOKEN, row_offset=rank * per_rank,
                                     workspace=wsp, best_key=key, tok=tok)
 
-    def max_ms(ms):
-        if world == 1:
-            return ms
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     # every rank replays its own graph (C3_CALLS tokens' lm_head calls, chained by
     # programmatic dependent launch as in a captured decode loop); the exchange
     # kernel meets the other ranks once per call
-    ms, g = time_graph(torch, lambda: [c3() for _ in range(C3_CALLS)], steps, warmup,
-                       (lambda: dist.barrier()) if world > 1 else None)
+    ms, g = time_graph(torch, lambda: [c3() for _ in range(C3_CALLS)], steps, warmup, sync_all)
     del g
+    # a peer that missed an exchange leaves only the device error word set: raise
+    ops.device_error()
     ms = max_ms(ms) / C3_CALLS
     ms_nccl = None
     if comm is not None:
@@ -353,8 +361,12 @@ def run_extras(torch, ops, dev, steps, warmup, world, rank, dist):
         e1.record()
         torch.cuda.synchronize()
         ms_nccl = max_ms(e0.elapsed_time(e1) / steps)
+    c3_parity = None
+    if world > 1:
+        c3_parity = c3_sharded_parity(torch, ops, dist, w, xq, xs, wsp, key, tok, rank, world, per_rank, c3,
+                                      c3_nccl)
     lm_bytes = gemv_bytes(k, vocab)
-    out["c3_lmhead_argmax"] = {"gpus": world, "us_per_token": round(ms * 1e3, 2), "tok_s": round(1e3 / ms, 1),
+    out["c3_lmhead_argmax"] = {"gpus": world, "c3_parity": c3_parity, "us_per_token": round(ms * 1e3, 2), "tok_s": round(1e3 / ms, 1),
                                "gbs_total": round(lm_bytes / (ms * 1e-3) / 1e9, 1),
                                "frac_hbm_per_gpu": round(lm_bytes / world / (ms * 1e-3) / 1e9 / hbm, 3),
                                "collective": "w4a8_lmhead_argmax_xchg: packed keys stored into every peer's "
@@ -393,6 +405,31 @@ def run_extras(torch, ops, dev, steps, warmup, world, rank, dist):
     c4["int8_peak_kind"] = "measured here: cuBLAS int8 GEMM (torch._int_mm) 8192^3, best of 5"
     out["c4_prefill_gemm"] = c4
     return out
+
+
+def c3_sharded_parity(torch, ops, dist, w, xq, xs, wsp, key, tok, rank, world, per_rank, c3, c3_nccl):
+    """The sharded lm_head's result on every rank against the max of the per-shard
+    keys: each rank's own shard key (plain fused argmax, no exchange) is gathered
+    over torch.distributed and the max taken on the host; the peer-memory exchange
+    (c3) and the NCCL all-reduce variant (c3_nccl) must both return that key and its
+    token on every rank.  Returns True only if they do on all ranks."""
+    own, _ = ops.lmhead_argmax(w, xq, xs, act=ops.ACT_TOKEN, row_offset=rank * per_rank, workspace=wsp)
+    gathered = [torch.empty_like(own) for _ in range(world)]
+    dist.all_gather(gathered, own)
+    mask = (1 << 64) - 1
+    ref_key = max(int(g.item()) & mask for g in gathered)
+    ref_tok = (~ref_key) & 0xFFFFFFFF if ref_key else 0
+    ok = True
+    for fn in (c3, c3_nccl):
+        key.zero_()
+        tok.fill_(-1)
+        fn()
+        torch.cuda.synchronize()
+        ops.device_error()
+        ok = ok and (int(key.item()) & mask) == ref_key and int(tok.item()) == ref_tok
+    flag = torch.tensor([1 if ok else 0], device=key.device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    return bool(flag.item())
 
 
 # ---------------------------------------------------------------------------
@@ -680,6 +717,9 @@ def main():
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+    c3p = (extras or {}).get("c3_lmhead_argmax", {}).get("c3_parity")
+    if c3p is False:
+        raise SystemExit("c3_parity: the sharded lm_head's key differs from the max of the shard keys")
 
 
 if __name__ == "__main__":

@@ -15,11 +15,10 @@
  *  - Errors are returned as a w4a8_status; w4a8_last_error() gives a message for
  *    the calling thread.  Shapes, modes and pointer alignment are validated on the
  *    host before any launch, so an EINVAL call launches nothing.
- *  - Calls on distinct streams are thread-safe.
- *  - One GPU per process: each kernel's shared-memory limit is raised once per
- *    process, at its first call, on the device current then.  A process that
- *    drives several GPUs gets W4A8_ECUDA from larger calls on the others.  Run one
- *    process per GPU, as torch.distributed and NCCL ranks do.
+ *  - Calls on distinct streams are thread-safe, and one process may drive several
+ *    GPUs: a call runs on the calling thread's current device, and each kernel's
+ *    launch state (its raised shared-memory limit, its occupancy figure) is kept
+ *    per device and set under a lock by the first call on that device.
  *
  * Weight layout (tools/convert.py:7-12, 68-75 of the reference): a quantized linear
  * weight with n output rows and k inputs is
@@ -226,9 +225,12 @@ W4A8_API w4a8_status w4a8_nccl_comm_destroy(void* comm);
  * double-buffered by the sequence's parity and the sequence counter lives on the
  * device, so the calls can be captured in a CUDA graph; every rank must make the
  * same number of calls with the same m (<= W4A8_XCHG_MAX_TOKENS).  A wait that
- * gives up leaves this rank's own keys in best_key and sets the device error word
- * (w4a8_device_error reports W4A8_ETIMEOUT).  No counterpart in the reference: this is
- * the exchange step of a column-split head, done over peer memory. */
+ * gives up (a peer ~0.3 s late, e.g. stalled on its host) leaves this rank's own
+ * keys in best_key and sets the device error word, and the call itself still
+ * returns W4A8_OK: callers must check w4a8_device_error (W4A8_ETIMEOUT) after their
+ * exchange calls, at the latest before they trust a token (a synchronizing check,
+ * so once per step or per batch of steps).  No counterpart in the reference: this
+ * is the exchange step of a column-split head, done over peer memory. */
 #define W4A8_XCHG_HANDLE_BYTES 64
 #define W4A8_XCHG_MAX_RANKS 8
 #define W4A8_XCHG_MAX_TOKENS 16

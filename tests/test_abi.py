@@ -64,6 +64,36 @@ def test_calls_reject_bad_arguments_before_launch():
     assert b"row_offset" in L.w4a8_last_error()
 
 
+def test_noalloc_rejects_bad_arguments_before_launch():
+    """w4a8_lmhead_argmax_noalloc runs the same checks as the workspace entry
+    point, before it touches the device: per-32 scales read as 8-byte pairs, so an
+    xs only 4-byte aligned is rejected, and so are a misaligned xq, a bad weight
+    and m beyond the library scratch's 16 tokens."""
+    L = _lib.load()
+    _, w = _view()
+    P = ctypes.c_void_p
+    key = P(64)
+    # act = GROUP32 with xs at 4 mod 8
+    assert L.w4a8_lmhead_argmax_noalloc(ctypes.byref(w), 0, P(16), P(20), 0, 1, None, key, None, None,
+                                        None) == _lib.EINVAL
+    assert b"xs misaligned" in L.w4a8_last_error()
+    # the same xs is fine for per-token scales (4-byte floats)... up to the device
+    # set-up, which this CPU test does not reach: check the other rejections instead
+    assert L.w4a8_lmhead_argmax_noalloc(ctypes.byref(w), 0, P(24), P(16), 0, 1, None, key, None, None,
+                                        None) == _lib.EINVAL
+    assert b"xq not 16-byte aligned" in L.w4a8_last_error()
+    bad = _lib.Weight(P(8).value, P(16).value, 8, 256, 32, 1)  # q misaligned
+    assert L.w4a8_lmhead_argmax_noalloc(ctypes.byref(bad), 0, P(16), P(16), 0, 1, None, key, None, None,
+                                        None) == _lib.EINVAL
+    assert L.w4a8_lmhead_argmax_noalloc(ctypes.byref(w), 0, P(16), P(16), 0, 17, None, key, None, None,
+                                        None) == _lib.EINVAL
+    assert b"16 tokens" in L.w4a8_last_error()
+    assert L.w4a8_lmhead_argmax_noalloc(ctypes.byref(w), 0, P(16), P(16), 0, 1, None, None, None, None,
+                                        None) == _lib.EINVAL
+    assert L.w4a8_lmhead_argmax_noalloc(ctypes.byref(w), -3, P(16), P(16), 0, 1, None, key, None, None,
+                                        None) == _lib.EINVAL
+
+
 def test_manifest_roundtrip_and_faults(tmp_path):
     codes = np.random.default_rng(0).integers(0, 16, (16, 64), dtype=np.uint32)
     q = fmt.pack_nibbles(codes)

@@ -1,5 +1,6 @@
-"""The column-split lm_head on 2 GPUs (one rank per GPU): each rank holds half of
-the vocabulary rows and the keys are exchanged (a) through torch.distributed NCCL
+"""The column-split lm_head on every GPU of the box (2 to 8, one rank per GPU): each
+rank holds a contiguous shard of the vocabulary rows (the vocabulary is not a
+multiple of the world size, so shards differ in size) and the keys are exchanged (a) through torch.distributed NCCL
 (ops.lmhead_argmax_sharded), (b) inside the library (w4a8_lmhead_argmax_allreduce
 over its own NCCL communicator) and (c) over peer memory (w4a8_lmhead_argmax_xchg:
 three calls, so both halves of the double-buffered key slots are used, then two
@@ -24,7 +25,13 @@ from helpers import make_weight, make_x, shard_key, to_i64
 
 pytestmark = pytest.mark.gpu
 
-V, K, M = 8192, 2048, 3
+V, K, M = 8192 + 8 * 3 + 5, 2048, 3  # not a multiple of any world size 2..8
+WORLD = min(torch.cuda.device_count(), 8)
+
+
+def _shard(rank, world):
+    """Rows [lo, hi) of rank's vocabulary shard (contiguous, sizes differ by <= 1)."""
+    return rank * V // world, (rank + 1) * V // world
 
 
 def _free_port():
@@ -53,10 +60,10 @@ def _rank(rank, world, port, results):
     from webyiq_b200._lib import ETIMEOUT, W4A8Error
 
     q, s, xq, xs = _data()
-    per = V // world
-    lo = rank * per
-    qt = torch.from_numpy(np.ascontiguousarray(q[lo:lo + per]).view(np.int32)).to(dev)
-    st = torch.from_numpy(np.ascontiguousarray(s[lo:lo + per]).view(np.int16)).to(dev)
+    lo, hi = _shard(rank, world)
+    per = hi - lo
+    qt = torch.from_numpy(np.ascontiguousarray(q[lo:hi]).view(np.int32)).to(dev)
+    st = torch.from_numpy(np.ascontiguousarray(s[lo:hi]).view(np.int16)).to(dev)
     w = ops.QWeight(qt, st, per, K, 128, False)
     xq_d, xs_d = torch.from_numpy(xq).to(dev), torch.from_numpy(xs).to(dev)
     key1, tok1 = ops.lmhead_argmax_sharded(w, xq_d, xs_d, lo, act=ops.ACT_TOKEN)
@@ -96,7 +103,7 @@ def _rank(rank, world, port, results):
     err = ops.device_error()
     del g
     dist.barrier()
-    # failure detection: rank 0 makes one more call that rank 1 never joins; its
+    # failure detection: rank 0 makes one more call that no other rank joins; its
     # bounded flag wait gives up, it keeps its own shard's key and the context
     # stays usable
     timeout_seen = None
@@ -119,9 +126,9 @@ def _rank(rank, world, port, results):
     dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_lmhead_split_two_gpus(cuda):
-    world = 2
+@pytest.mark.skipif(WORLD < 2, reason="needs 2 GPUs")
+def test_lmhead_split_all_gpus(cuda):
+    world = WORLD
     port = _free_port()
     with mp.get_context("spawn").Manager() as mgr:
         results = mgr.dict()

@@ -19,21 +19,35 @@ namespace {
 thread_local char t_err[512] = "";
 }  // namespace
 
-int sm_count() {
-    static int counts[64] = {0};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-    if (counts[dev] == 0) {
-        int n = 0;
-        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-        counts[dev] = n;
+int current_device(const char* what) {
+    int dev = -1;
+    const cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        set_error(W4A8_ECUDA, "%s: cudaGetDevice: %s", what, cudaGetErrorString(e));
+        return -1;
     }
-    return counts[dev];
+    if (dev < 0 || dev >= kMaxDevices) {
+        set_error(W4A8_ECUDA, "%s: device %d beyond the library's %d", what, dev, kMaxDevices);
+        return -1;
+    }
+    return dev;
 }
 
-namespace {
+// SMs of the current device, read once per device (benign race: every thread that
+// reads it first stores the same value).
+int sm_count() {
+    static std::atomic<int> counts[kMaxDevices];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+    int n = counts[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        counts[dev].store(n, std::memory_order_relaxed);
+    }
+    return n;
+}
+
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
-}  // namespace
 
 w4a8_status set_error(w4a8_status st, const char* fmt, ...) {
     va_list ap;
@@ -87,8 +101,7 @@ w4a8_status launch_gemv(const GemvParams& p, int group, bool has_min, int act, i
     return has_min ? launch_gemv_g128_m1(p, act, mode, out, st) : launch_gemv_g128_m0(p, act, mode, out, st);
 }
 
-namespace {
-
+// Argument checks shared by every entry point that takes a weight or activations.
 w4a8_status check_weight(const w4a8_weight* w, const char* what) {
     if (!w) return set_error(W4A8_EINVAL, "%s: weight is NULL", what);
     if (!w->q || !w->s) return set_error(W4A8_EINVAL, "%s: weight pointers are NULL", what);
@@ -111,7 +124,6 @@ w4a8_status check_act(const int8_t* xq, const float* xs, int act, const char* wh
     return W4A8_OK;
 }
 
-}  // namespace
 }  // namespace w4a8
 
 using namespace w4a8;

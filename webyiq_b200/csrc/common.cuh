@@ -14,6 +14,12 @@ namespace w4a8 {
 // Host-side status helpers (defined in capi.cu)
 w4a8_status set_error(w4a8_status st, const char* fmt, ...);
 w4a8_status check_launch(const char* what);
+// Argument checks of the entry points (EINVAL with a message naming `what`): a
+// weight view's group, shape and pointer alignment; activation pointers, layout
+// and alignment (xq 16 bytes, xs 8 bytes for W4A8_ACT_GROUP32, else 4).
+w4a8_status check_weight(const w4a8_weight* w, const char* what);
+w4a8_status check_act(const int8_t* xq, const float* xs, int act, const char* what);
+bool aligned(const void* p, size_t a);
 
 constexpr int kWarp = 32;
 constexpr unsigned kFull = 0xffffffffu;

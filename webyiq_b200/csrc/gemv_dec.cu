@@ -449,15 +449,11 @@ bool dec_plan(const GemvParams& g, bool has_min, int mode, DecPlan& pl) {
 
 template <bool HAS_MIN, int MODE, int MT, int GPL, bool FQ, bool NORM, bool DEEP>
 w4a8_status dec_inst(const DecParams& p, const DecPlan& pl, cudaStream_t st) {
-    static size_t configured = 0;  // set on first use: static shared memory counts against the default 48 KB too
+    // set on first use per device: static shared memory counts against the default 48 KB too
+    static FuncAttr attr;
     auto kernel = gemv_dec_kernel<HAS_MIN, MODE, MT, GPL, FQ, NORM, DEEP>;
-    if (pl.smem > configured) {
-        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pl.smem));
-        if (e != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8 gemv (decode): smem attribute: %s", cudaGetErrorString(e));
-        const cudaError_t c = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-        if (c != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8 gemv (decode): carveout: %s", cudaGetErrorString(c));
-        configured = pl.smem;
-    }
+    const w4a8_status a = ensure_smem(kernel, attr, pl.smem, 100, "w4a8 gemv (decode)");
+    if (a != W4A8_OK) return a;
     return launch_pdl("w4a8 gemv (decode)", kernel, dim3(pl.ctas), dim3(DecCfg<MT, GPL, DEEP>::threads), pl.smem, st, p);
 }
 

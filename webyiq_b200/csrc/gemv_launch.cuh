@@ -12,17 +12,14 @@ int sm_count();  // capi.cu
 // Launch plan: 2 CTAs per SM on balanced contiguous row ranges of at least 4
 // rows (fewer CTAs when rows are scarce); T = a multiple of k/32 threads.
 template <typename Kernel>
-w4a8_status launch_gemv_kernel(Kernel kernel, size_t& configured, GemvParams p, int group, int nr,
-                               cudaStream_t st) {
+w4a8_status launch_gemv_kernel(Kernel kernel, FuncAttr& attr, GemvParams p, int group, int nr, cudaStream_t st) {
     const int kc = p.k / 32;
     if (kc > kGemvMaxKC) return set_error(W4A8_EINVAL, "w4a8 gemv: k=%d too large (max %d)", p.k, kGemvMaxKC * 32);
     const int threads = gemv_threads(kc);
     const size_t smem = gemv_smem_bytes(p.m, p.k, group, nr);
-    if (smem > configured) {  // `configured` belongs to this one kernel instantiation
-        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   static_cast<int>(smem));
-        if (e != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8 gemv: smem attribute: %s", cudaGetErrorString(e));
-        configured = smem;
+    if (smem > 48 * 1024) {  // `attr` belongs to this one kernel instantiation
+        const w4a8_status a = ensure_smem(kernel, attr, smem, -1, "w4a8 gemv");
+        if (a != W4A8_OK) return a;
     }
     const int sms = sm_count();
     int ctas = 2 * sms;
@@ -33,8 +30,8 @@ w4a8_status launch_gemv_kernel(Kernel kernel, size_t& configured, GemvParams p, 
 
 template <int G, bool HAS_MIN, int ACT, int MODE, int MT, int OUT>
 w4a8_status launch_gemv_inst(const GemvParams& p, cudaStream_t st) {
-    static size_t configured = 48 * 1024;  // dynamic smem this instantiation may use
-    return launch_gemv_kernel(gemv_kernel<G, HAS_MIN, ACT, MODE, MT, OUT>, configured, p, G,
+    static FuncAttr attr;  // dynamic smem this instantiation may use, per device
+    return launch_gemv_kernel(gemv_kernel<G, HAS_MIN, ACT, MODE, MT, OUT>, attr, p, G,
                               MODE == W4A8_SWIGLU ? 2 : 1, st);
 }
 

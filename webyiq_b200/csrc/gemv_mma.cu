@@ -12,7 +12,7 @@ namespace {
 // RT tiles of 16 rows (8 output rows for SWIGLU); RT x KS warps, KS = ceil(KG/4).
 template <bool HAS_MIN, int MODE, int OUT, int MT, bool FQ>
 w4a8_status launch_mt(MmaParams p, cudaStream_t st) {
-    static size_t configured = 0;  // set on first use: static shared memory counts against the default 48 KB too
+    static FuncAttr attr;  // set on first use per device: static shared memory counts against the default 48 KB too
     auto kernel = gemv_mma_kernel<HAS_MIN, MODE, OUT, MT, FQ>;
     const int kg = p.k / 128;
     p.ks = (kg + kMmaGPS - 1) / kMmaGPS;
@@ -34,12 +34,8 @@ w4a8_status launch_mt(MmaParams p, cudaStream_t st) {
     while (plan.total > 227 * 1024 && p.stages > 1) plan = mma_smem_plan(p.m, p.k, p.rt, p.ks, --p.stages, sb);
     while (plan.total > 227 * 1024 && p.rt > 1) plan = mma_smem_plan(p.m, p.k, --p.rt, p.ks, p.stages, sb);
     if (plan.total > 227 * 1024) return set_error(W4A8_EINVAL, "w4a8 gemv: shared memory plan too large");
-    if (plan.total > configured) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan.total));
-        if (e != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8 gemv: smem attribute: %s", cudaGetErrorString(e));
-        configured = plan.total;
-    }
+    const w4a8_status a = ensure_smem(kernel, attr, plan.total, -1, "w4a8 gemv (mma)");
+    if (a != W4A8_OK) return a;
     return launch_pdl("w4a8 gemv (mma)", kernel, dim3(ctas), dim3(p.rt * p.ks * 32), plan.total, st, p);
 }
 
@@ -135,15 +131,17 @@ w4a8_status selftest_wait_timeout(cudaStream_t st) {
 // Device address of the error word, for kernels compiled in other files (each
 // file has its own __device__ variables, so they take it as a parameter).
 unsigned int* device_error_word() {
-    static unsigned int* addr[64] = {nullptr};
+    static std::atomic<unsigned int*> addr[kMaxDevices];
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    if (!addr[dev]) {
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    unsigned int* a = addr[dev].load(std::memory_order_acquire);
+    if (!a) {  // every thread that resolves it first stores the same address
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_w4a8_dev_error) != cudaSuccess) return nullptr;
-        addr[dev] = static_cast<unsigned int*>(p);
+        a = static_cast<unsigned int*>(p);
+        addr[dev].store(a, std::memory_order_release);
     }
-    return addr[dev];
+    return a;
 }
 
 w4a8_status device_error(unsigned int* code, cudaStream_t st) {

@@ -33,17 +33,17 @@ namespace {
 
 constexpr size_t kScratchBytes = sizeof(g_lmhead_scratch);
 constexpr int kScratchTokens = 16;
-constexpr int kMaxDevices = 64;
+constexpr int kScratchDevices = 64;
 
 std::mutex g_setup_mutex;
-void* g_scratch_addr[kMaxDevices] = {nullptr};
+void* g_scratch_addr[kScratchDevices] = {nullptr};
 
 // Device address of this device's scratch array (set-up on first use).
 w4a8_status scratch_for_current_device(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8_lmhead_argmax_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
-    if (dev < 0 || dev >= kMaxDevices) return set_error(W4A8_EINVAL, "w4a8_lmhead_argmax_noalloc: device %d", dev);
+    if (dev < 0 || dev >= kScratchDevices) return set_error(W4A8_EINVAL, "w4a8_lmhead_argmax_noalloc: device %d", dev);
     std::lock_guard<std::mutex> lock(g_setup_mutex);
     if (!g_scratch_addr[dev]) {
         void* ptr = nullptr;
@@ -72,19 +72,14 @@ extern "C" W4A8_API w4a8_status w4a8_lmhead_argmax_noalloc(const w4a8_weight* w,
         return set_error(W4A8_EINVAL,
                          "w4a8_lmhead_argmax_noalloc: m=%d exceeds the %d tokens its %zu-byte scratch holds", m,
                          kScratchTokens, kScratchBytes);
-    if (!w || !w->q || !w->s || (w->group != 32 && w->group != 128) || w->k <= 0 || w->k % w->group || w->n <= 0)
-        return set_error(W4A8_EINVAL, "w4a8_lmhead_argmax_noalloc: bad weight");
-    if (!xq || !xs || (act != W4A8_ACT_GROUP32 && act != W4A8_ACT_TOKEN))
-        return set_error(W4A8_EINVAL, "w4a8_lmhead_argmax_noalloc: bad activations");
-    if ((reinterpret_cast<uintptr_t>(xq) & 15) || (reinterpret_cast<uintptr_t>(w->q) & 15) ||
-        (reinterpret_cast<uintptr_t>(w->s) & 3))
-        return set_error(W4A8_EINVAL, "w4a8_lmhead_argmax_noalloc: misaligned pointer");
+    w4a8_status st = check_weight(w, "w4a8_lmhead_argmax_noalloc");
+    if (st != W4A8_OK) return st;
+    if ((st = check_act(xq, xs, act, "w4a8_lmhead_argmax_noalloc")) != W4A8_OK) return st;
     if (!best_key) return set_error(W4A8_EINVAL, "w4a8_lmhead_argmax_noalloc: best_key is NULL");
     if (m < 1) return set_error(W4A8_EINVAL, "w4a8_lmhead_argmax_noalloc: m=%d", m);
     if (row_offset < 0) return set_error(W4A8_EINVAL, "w4a8_lmhead_argmax_noalloc: row_offset=%d", row_offset);
     void* scratch = nullptr;
-    const w4a8_status st = scratch_for_current_device(&scratch);
-    if (st != W4A8_OK) return st;
+    if ((st = scratch_for_current_device(&scratch)) != W4A8_OK) return st;
     GemvParams p{};
     p.q = static_cast<const uint4*>(w->q);
     p.s = w->s;

@@ -281,16 +281,17 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_stream_kernel(const Stream
         }
     }
     __syncthreads();
-    if (s_abort) {
+    const bool aborted = s_abort;
+    if (aborted && tid == 0) {
         // no copy may still be landing when the CTA exits
-        if (tid == 0)
-            for (int j = s_issued > kStages ? s_issued - kStages : 0; j < s_issued; ++j)
-                mbar_wait(&full[j % kStages], (j / kStages) & 1);
-        return;
+        for (int j = s_issued > kStages ? s_issued - kStages : 0; j < s_issued; ++j)
+            mbar_wait(&full[j % kStages], (j / kStages) & 1);
     }
 
-    // CTA max, one atomicMax per token, the last CTA publishes and re-zeroes.
-    if (tid < p.m) {
+    // CTA max, one atomicMax per token, the last CTA publishes and re-zeroes.  A CTA
+    // whose wait gave up adds no key but is still counted, so the workspace is left
+    // zeroed for the next call whatever happened in this one.
+    if (!aborted && tid < p.m) {
         unsigned long long key = 0;
         for (int w = 0; w < kConsumers; ++w) {
             const unsigned long long o = s_key[w][tid];
@@ -321,14 +322,11 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_stream_kernel(const Stream
 
 template <bool HAS_MIN, int MT, int L, int GPL>
 w4a8_status launch_inst(const StreamParams& p, cudaStream_t st) {
-    static size_t configured = 0;
+    static FuncAttr attr;
     auto kernel = lmhead_stream_kernel<HAS_MIN, MT, L, GPL>;
     const size_t smem = static_cast<size_t>(kStages) * p.stage_bytes;
-    if (smem > configured) {
-        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        if (e != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8 lm_head (stream): smem attribute: %s", cudaGetErrorString(e));
-        configured = smem;
-    }
+    const w4a8_status a = ensure_smem(kernel, attr, smem, -1, "w4a8 lm_head (stream)");
+    if (a != W4A8_OK) return a;
     int ctas = sm_count();
     const int nblk = p.n / 8;
     if (ctas > nblk) ctas = nblk;

@@ -277,9 +277,15 @@ class PeerExchange:
 
 
 def lmhead_argmax_xchg(w, xq, xs, xchg, act=ACT_TOKEN, row_offset=0, logits=None, ids=None, workspace=None,
-                       best_key=None, tok=None):
+                       best_key=None, tok=None, check=False):
     """Sharded lm_head with the key exchange over peer memory (PeerExchange) instead
-    of NCCL.  Returns (best_key int64 [m], tok int32 [m]) of the global argmax."""
+    of NCCL.  Returns (best_key int64 [m], tok int32 [m]) of the global argmax.
+
+    A peer that does not join within the exchange's bounded wait leaves this rank's
+    own shard key in best_key, and only the device error word records it: with
+    check=True the call synchronizes the stream and raises W4A8Error (ETIMEOUT) in
+    that case; otherwise call device_error() before trusting the tokens (not inside
+    a stream capture)."""
     _need_cuda(xq, xs, logits, ids, workspace)
     m = xq.shape[0]
     dev = xq.device
@@ -292,6 +298,8 @@ def lmhead_argmax_xchg(w, xq, xs, xchg, act=ACT_TOKEN, row_offset=0, logits=None
     _lib.check(_lib.load().w4a8_lmhead_argmax_xchg(ctypes.byref(w.c), int(row_offset), _ptr(xq), _ptr(xs), act, m,
                                                    _ptr(logits), _ptr(best_key), _ptr(tok), _ptr(ids),
                                                    _ptr(workspace), workspace.numel(), xchg.ptr, _stream()))
+    if check:
+        device_error()
     return best_key, tok
 
 
