@@ -21,30 +21,35 @@
 //  - Weight rows are the MMA M (one TMEM lane per row), tokens the MMA N: the
 //    per-group scale s[n, g] is a per-lane constant in the epilogue.
 //  - The packed weights arrive by TMA (a 3-D map of 4 groups x 128 rows x 64 B with
-//    64-byte swizzle, so the row reads are conflict-free).  The epilogue warps
-//    expand each group kLead groups ahead of its MMA into an int8 weight tile in
-//    TMEM (the MMA's A operand): 16*(q-8) per byte, the nibble q^8 (the 4-bit
+//    64-byte swizzle, so the row reads are conflict-free).  The expansion warps
+//    expand each group ahead of its MMA into an int8 weight tile in TMEM (the
+//    MMA's A operand): 16*(q-8) per byte, the nibble q^8 (the 4-bit
 //    two's complement of q-8) in the high half of the byte, so its sign extends
 //    for free; the factor 16 is folded into the scale (exact).  Keeping A in TMEM
 //    spares shared-memory bandwidth, the other limit of this kernel.
 //  - Activations come by TMA, four groups (4 x 8 KB) per copy through a 3-D
 //    tensor map (k-inner 128 bytes, tokens, groups), so every group lands as its
 //    own swizzled K-major block (the MMA's B operand).
-//  - Each TMEM accumulator is pre-set to the bits of 1.5*2^23 and the MMA adds the
-//    group's dots onto it (|16 I| < 2^22), so the accumulator read back as a float
-//    is exactly 1.5*2^23 + 16 I; one packed subtract and one packed FMA per two
-//    values finish the scale step, and writing the bias back re-arms the buffer.
-//    Three accumulator buffers of 128 columns and four int8 weight tiles of 32
-//    columns fill TMEM's 512 columns.
+//  - Each group's MMAs write their own TMEM accumulator (the first k-step
+//    overwrites it), an exact int32 16 I.  The scale warps read it, release the
+//    buffer at once and finish the scale step from registers (an exact int -> f32
+//    conversion and one packed FMA per two values).  Three accumulator buffers of
+//    128 columns and four int8 weight tiles of 32 columns fill TMEM's 512 columns.
 //
-// Warp roles per CTA (10 warps, 168 registers each): 0 weight and activation TMA,
-// 1 MMA issue (cluster rank 0 only; a tcgen05.mma blocks its thread for about its
-// own duration) and TMEM allocation, 2-9 epilogue: int4 -> int8 expansion kLead
-// groups ahead and the scale step (two halves of 64 columns; warp % 4 is the TMEM
-// lane quadrant a warp may access).
-// Barriers that the MMA waits on (int8 tiles written, accumulators released)
-// live in rank 0 and both CTAs arrive on them; the MMA's completions arrive on
-// both CTAs' barriers (one tcgen05.commit per CTA).  Every wait is bounded; a wait
+// Warp roles per CTA (23 warps): 0 weight and activation TMA; 1 and 2 MMA issue
+// (cluster rank 0 only), the even and the odd groups (a tcgen05.mma blocks its
+// thread for about its own duration, and a barrier test or commit after it holds
+// the thread up further, so a second issuing thread keeps the tensor core fed
+// meanwhile); 1 also allocates TMEM; 3-6 weight expansion, one warp per TMEM lane
+// quarter (warp % 4 is the quarter a warp may access), each thread expanding its
+// whole tile row of a group into the TMEM weight tile, up to kABufs groups ahead
+// of the scale step; 7-22 the scale step, four warps per lane quarter, each on its
+// own 32 of the tile's 128 token columns.  Expansion and scale step run in
+// separate warps so neither waits behind the other, and four scale warps per SM
+// sub-partition hide the TMEM load latency of each other.
+// The barrier the MMA waits on per group ("go": its int8 tile written and its
+// accumulator released) lives in rank 0 and both CTAs arrive on it; the MMA's
+// completions arrive on both CTAs' barriers (one multicast tcgen05.commit).  Every wait is bounded; a wait
 // that gives up sets the device error word and all roles then leave their loops.
 // Nothing here uses cluster multicast.
 #include <cuda.h>
@@ -71,15 +76,17 @@ constexpr int kSG = 4;          // groups per pipeline stage (one weight and one
 constexpr int kStages = 3;
 constexpr int kDBufs = 3;       // TMEM group accumulators of kTok columns
 constexpr int kABufs = 4;       // TMEM int8 weight tiles of 32 columns (128 rows x 128 k)
-constexpr int kLead = 2;        // groups the weight expansion runs ahead of the scale step
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA = kDBufs * kTok;  // first column of the weight tiles
 static_assert(kTmemA + kABufs * 32 <= kTmemCols, "TMEM plan exceeds 512 columns");
-static_assert(kLead < kABufs && kLead < kDBufs + 1, "expansion lead exceeds the buffers");
-constexpr int kEpiWarp0 = 2, kEpiWarps = 8;
-constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 320 (allocated as 384: 168 registers a thread)
-constexpr uint32_t kBias = 0x4B400000u;                  // bits of 1.5 * 2^23
-constexpr float kBiasF = 12582912.0f;
+constexpr int kMmaWarps = 2;                 // MMA issue: warp 1 the even groups, warp 2 the odd ones
+constexpr int kExpWarp0 = 1 + kMmaWarps, kExpWarps = 4;  // weight expansion: one warp per TMEM lane quarter
+constexpr int kSclWarp0 = kExpWarp0 + kExpWarps;
+constexpr int kSclPerQuad = 4;                          // scale warps per lane quarter
+constexpr int kSclWarps = 4 * kSclPerQuad;
+constexpr int kCW = kTok / kSclPerQuad;                 // token columns of one scale warp
+static_assert(kCW == 32, "a scale warp reads its slice of an accumulator with one 32-column load");
+constexpr int kThreads = (kSclWarp0 + kSclWarps) * 32;  // 736 (80 registers a thread)
 
 constexpr uint32_t kWGroupBytes = kRows * 64;       // packed weights of one group (this CTA's rows)
 constexpr uint32_t kXGroupBytes = kHalfTok * 128;   // activations of one group (this CTA's tokens)
@@ -87,7 +94,7 @@ constexpr uint32_t kStageBytes = kSG * (kWGroupBytes + kXGroupBytes);
 constexpr uint32_t kOffW = 0;                       // [stage][group][128 rows][64 B], 64-byte swizzle
 constexpr uint32_t kOffX = kStages * kSG * kWGroupBytes;  // [stage][group][64 tokens][128 B], 128-byte swizzle
 constexpr uint32_t kOffXchg = kOffX + kStages * kSG * kXGroupBytes;
-constexpr uint32_t kXchgBytes = 2 * 64 * 64 * 4;  // SWIGLU: up-half values of both column halves
+constexpr uint32_t kXchgBytes = kTok * 64 * 4;  // SWIGLU: up-row values of every column slice
 
 __host__ __device__ constexpr uint32_t bar_offset(bool swiglu) { return kOffXchg + (swiglu ? kXchgBytes : 0); }
 __host__ __device__ constexpr size_t smem_bytes(bool swiglu) { return 1024 + bar_offset(swiglu) + 512; }
@@ -158,12 +165,14 @@ constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<ui
                             (static_cast<uint32_t>(256 >> 4) << 24);
 
 // One k-step of the pair's MMA: A (this CTA's 128 weight rows, int8) from TMEM,
-// B (this CTA's 64 tokens) from shared memory.
-__device__ __forceinline__ void mma_i8_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc) {
+// B (this CTA's 64 tokens) from shared memory; acc = 0 overwrites the
+// accumulator (the group's first k-step), acc = 1 adds to it.
+__device__ __forceinline__ void mma_i8_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t acc) {
     asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, 1, 0;\n"
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::2.kind::i8 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(bdesc), "r"(idesc)
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(acc)
         : "memory");
 }
 // Arrives on the barrier at this shared::cluster address (either CTA of the pair)
@@ -172,10 +181,14 @@ __device__ __forceinline__ void tc_commit_to(uint32_t cluster_addr) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
                  : "memory");
 }
-// The same barrier in both CTAs: one commit per CTA.
-__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
-    tc_commit_to(peer_addr(bar, 0));
-    tc_commit_to(peer_addr(bar, 1));
+// The same barrier in both CTAs, one instruction: the commit arrives at this
+// shared-memory offset in every CTA of the mask (both CTAs of the pair).  This is
+// a completion signal, not a load; nothing here loads with cluster multicast.
+__device__ __forceinline__ void tc_commit_both(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                     smem_u32(bar)),
+                 "h"(static_cast<unsigned short>(3))
+                 : "memory");
 }
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
     asm volatile(
@@ -200,22 +213,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// 16 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+// 32 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
         "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-        : "memory");
-}
-
-// Writes the bias into 32 consecutive columns of this thread's lane.
-__device__ __forceinline__ void tmem_bias32(uint32_t taddr) {
-    const uint32_t b = kBias;
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
-        "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-        "r"(b)
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
 }
 
@@ -233,9 +239,9 @@ struct Abort {
         return false;
     }
     __device__ bool wait(uint64_t* bar, uint32_t parity) const { return mbar_wait(bar, parity) || fail(); }
-    // Barrier over the 128 threads of one epilogue column half (bounded, unlike a
+    // Barrier over the 128 threads of one scale column slice (bounded, unlike a
     // named barrier).
-    __device__ bool half_sync(uint64_t* bar, uint32_t& phase) const {
+    __device__ bool slice_sync(uint64_t* bar, uint32_t& phase) const {
         asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
         const bool ok = mbar_wait(bar, phase & 1);
         ++phase;
@@ -252,14 +258,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + bar_offset(SWI));  // stage copies landed (local)
     uint64_t* empty = full + kStages;     // MMA done with a stage (both)
-    uint64_t* aready = empty + kStages;   // int8 weight tile written to TMEM (rank 0; both CTAs arrive)
+    // "Go" for group j (ring of kABufs, rank 0; both CTAs arrive): its int8 weight
+    // tile is in TMEM (the expansion warps' arrivals) and its accumulator buffer is
+    // free (the scale warps' arrivals after group j - kDBufs), so the MMA thread
+    // waits on one barrier per group.
+    uint64_t* go = empty + kStages;
     // The MMAs of group j complete (both CTAs, one ring of kABufs): accumulator j
     // may be read, and weight tile j % kABufs may be rewritten for group j + kABufs.
-    uint64_t* gdone = aready + kABufs;
-    uint64_t* acce = gdone + kABufs;      // accumulator read and re-biased (rank 0; both arrive)
-    uint64_t* done = acce + kDBufs;       // all MMAs complete (rank 0)
-    uint64_t* xbar = done + 1;            // SWIGLU exchange, one per column half (local)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 2);
+    uint64_t* gdone = go + kABufs;
+    uint64_t* done = gdone + kABufs;      // all MMAs complete (rank 0)
+    uint64_t* xbar = done + 1;            // SWIGLU exchange, one per column slice (local)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + kSclPerQuad);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -267,16 +276,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(full + s, 1);
-            mbar_init(empty + s, 1);
+            mbar_init(empty + s, kMmaWarps);  // one commit per MMA thread
         }
         for (int a = 0; a < kABufs; ++a) {
-            mbar_init(aready + a, 2 * kEpiWarps);  // one arrival per epilogue warp of each CTA
+            mbar_init(go + a, 2 * (kExpWarps + kSclWarps));  // every expansion and scale warp of each CTA
             mbar_init(gdone + a, 1);
         }
-        for (int b = 0; b < kDBufs; ++b) mbar_init(acce + b, 2 * kEpiWarps);
-        mbar_init(done, 1);
-        mbar_init(xbar, 128);
-        mbar_init(xbar + 1, 128);
+        mbar_init(done, kMmaWarps);
+        for (int c = 0; c < kSclPerQuad; ++c) mbar_init(xbar + c, 128);
         *abort_flag = 0;
         mbar_init_fence();
     }
@@ -331,112 +338,113 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (uint32_t i = js > kStages ? js - kStages : 0; i < js; ++i)
                 mbar_wait(full + i % kStages, (i / kStages) & 1);
         }
-    } else if (warp == 1) {
-        // ---- MMA issue (rank 0): four k-steps of 32 per group for the pair ----
-        // (Both CTAs' epilogue threads saw the group's stage land before they
-        // arrived on aready, so aready covers the activation tile halves too.)
+    } else if (warp <= kMmaWarps) {
+        // ---- MMA issue (rank 0): four k-steps of 32 per group for the pair, the
+        //      even groups from warp 1 and the odd ones from warp 2 ----
+        // (Both CTAs' expansion warps saw the group's stage land before they
+        // arrived on go, so go covers the activation tile halves too.)  A barrier
+        // test or a commit right after MMAs holds up its thread for about 200 / 60
+        // cycles, in which this thread's own MMAs drain; with two threads issuing
+        // alternate groups, one thread's test and commit run while the other's MMAs
+        // keep the tensor core busy.  Each thread commits only its own MMAs (a
+        // commit tracks the MMAs its thread issued), so every group's completion
+        // and every stage's release (count kMmaWarps) stay exact.
         if (rank == 0 && lane == 0) {
+            const uint32_t par = static_cast<uint32_t>(warp - 1);  // this thread's groups: j % 2 == par
             uint32_t j = 0, js = 0;
             bool ok = true;
             for (int i = 0; i < my_tiles && ok; ++i) {
                 for (int g = 0; g < kg; ++g, ++j) {
                     const uint32_t s = js % kStages;
-                    const uint32_t a = j % kABufs, ua = j / kABufs;
-                    const uint32_t b = j % kDBufs, v = j / kDBufs;
-                    if (*abort_flag || !ab.wait(aready + a, ua & 1) || !ab.wait(acce + b, v & 1)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t x_addr = smem_u32(smem + kOffX + (s * kSG + g % kSG) * kXGroupBytes);
-                    const uint32_t d = tmem + b * kTok;
-                    const uint32_t at = tmem + kTmemA + a * 32;
+                    if ((j & 1) == par) {
+                        const uint32_t a = j % kABufs, ua = j / kABufs;
+                        const uint32_t b = j % kDBufs;
+                        if (!mbar_test(go + a, ua & 1) && (*abort_flag || !ab.wait(go + a, ua & 1))) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t x_addr = smem_u32(smem + kOffX + (s * kSG + g % kSG) * kXGroupBytes);
+                        const uint32_t d = tmem + b * kTok;
+                        const uint32_t at = tmem + kTmemA + a * 32;
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) mma_i8_pair_ts(d, at + kk * 8, sw128_desc(x_addr + 32 * kk), kIdesc);
-                    tc_commit_pair(gdone + a);
+                        for (int kk = 0; kk < 4; ++kk)
+                            mma_i8_pair_ts(d, at + kk * 8, sw128_desc(x_addr + 32 * kk), kIdesc, kk > 0);
+                        tc_commit_both(gdone + a);
+                    }
                     if (g % kSG == kSG - 1 || g == kg - 1) {
-                        tc_commit_pair(empty + s);
+                        tc_commit_both(empty + s);  // this thread's MMAs of the stage (none: at once)
                         ++js;
                     }
                 }
             }
             // Every MMA issued completes before TMEM is released.
             tc_commit_to(peer_addr(done, 0));
-            mbar_wait(done, 0);
+            if (warp == 1) mbar_wait(done, 0);
         }
-    } else if (warp >= kEpiWarp0) {
-        // ---- epilogue: weight expansion kLead groups ahead, scale step per group,
-        //      output per tile ----
-        const int ew = warp - kEpiWarp0;
-        const int quad = warp & 3, half = ew >> 2;
+    } else if (warp < kSclWarp0) {
+        // ---- weight expansion: every group of every tile, in order, into TMEM weight
+        //      tile jd % kABufs, as soon as its stage has landed and the MMAs that read
+        //      the tile's previous contents have completed ----
+        const int quad = warp & 3;
         const int lrow = quad * 32 + lane;  // TMEM lane = tile row of this thread
         const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-        const uint32_t d_base = tmem + lane_off + half * 64;
-        const uint32_t aready_rank0 = peer_addr(aready, 0);
-        const uint32_t acce_rank0 = peer_addr(acce, 0);
-        for (int b = 0; b < kDBufs; ++b) {
-            tmem_bias32(d_base + b * kTok);
-            tmem_bias32(d_base + b * kTok + 32);
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0)
-            for (int b = 0; b < kDBufs; ++b) arrive_cluster(acce_rank0 + b * 8);
-
+        const uint32_t go_rank0 = peer_addr(go, 0);
         const uint32_t total = static_cast<uint32_t>(my_tiles) * kg;
-        // The expansion walks the groups in order: group ge of tile ie, in stage sde
-        // (a running stage index), into TMEM weight tile jd % kABufs.
-        uint32_t jd = 0, sde = 0;
-        int ge = 0;
-        // Expands half (k 64*half .. +63) of this thread's weight row for the next
-        // group of the walk and stores it into the TMEM weight tile; the caller
-        // publishes it (wait::st, fence, arrival on aready) with its own stores.
-        uint32_t a_pub = 0;  // the tile the last expansion wrote
-        auto expand_issue = [&]() -> bool {
+        const int sw = (lrow >> 1) & 3;  // the 64-byte swizzle of this row's chunks
+        uint32_t sde = 0;                // running stage index
+        int ge = 0;                      // group within the tile
+        for (uint32_t jd = 0; jd < total; ++jd) {
             const uint32_t s = sde % kStages, a = jd % kABufs, ua = jd / kABufs;
-            const bool w_ok = ab.wait(full + s, (sde / kStages) & 1) && ab.wait(gdone + a, (ua & 1) ^ 1);
-            if (!__all_sync(kFull, w_ok)) return false;
-            // Packed row lrow of the group: 64 bytes, 16-byte chunks swizzled by (row/2)%4.
-            // A stage holds [kSG groups][128 rows][64 B]; for SWIGLU it holds two such
-            // boxes of 64 rows (gate rows, then up rows).
+            const bool w_ok = !*abort_flag && ab.wait(full + s, (sde / kStages) & 1) && ab.wait(gdone + a, (ua & 1) ^ 1);
+            if (!__all_sync(kFull, w_ok)) break;
+            // Packed row lrow of the group: 64 bytes in four 16-byte chunks, chunk c at
+            // (c ^ sw) * 16.  A stage holds [kSG groups][128 rows][64 B]; for SWIGLU two
+            // such boxes of 64 rows (gate rows, then up rows).
             const unsigned char* stage_w = smem + kOffW + s * kSG * kWGroupBytes;
             const unsigned char* wrow =
                 SWI ? stage_w + (lrow >= 64 ? kSG * kWGroupBytes / 2 : 0) + (ge % kSG) * (kWGroupBytes / 2) + (lrow & 63) * 64
                     : stage_w + (ge % kSG) * kWGroupBytes + lrow * 64;
-            const int sw = (lrow >> 1) & 3;
-            const uint4 c0 = *reinterpret_cast<const uint4*>(wrow + (((2 * half) ^ sw) << 4));
-            const uint4 c1 = *reinterpret_cast<const uint4*>(wrow + (((2 * half + 1) ^ sw) << 4));
-            const uint32_t v[16] = {expand_lo(c0.x), expand_hi(c0.x), expand_lo(c0.y), expand_hi(c0.y),
-                                    expand_lo(c0.z), expand_hi(c0.z), expand_lo(c0.w), expand_hi(c0.w),
-                                    expand_lo(c1.x), expand_hi(c1.x), expand_lo(c1.y), expand_hi(c1.y),
-                                    expand_lo(c1.z), expand_hi(c1.z), expand_lo(c1.w), expand_hi(c1.w)};
-            tmem_st16(tmem + lane_off + kTmemA + a * 32 + half * 16, v);
-            a_pub = a;
-            ++jd;
-            if (ge % kSG == kSG - 1 || ge == kg - 1) ++sde;
-            if (++ge == kg) ge = 0;
-            return true;
-        };
-        auto expand = [&]() -> bool {
-            if (!expand_issue()) return false;
+            uint32_t v[32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint4 ch = *reinterpret_cast<const uint4*>(wrow + ((c ^ sw) << 4));
+                v[8 * c + 0] = expand_lo(ch.x);
+                v[8 * c + 1] = expand_hi(ch.x);
+                v[8 * c + 2] = expand_lo(ch.y);
+                v[8 * c + 3] = expand_hi(ch.y);
+                v[8 * c + 4] = expand_lo(ch.z);
+                v[8 * c + 5] = expand_hi(ch.z);
+                v[8 * c + 6] = expand_lo(ch.w);
+                v[8 * c + 7] = expand_hi(ch.w);
+            }
+            tmem_st32(tmem + lane_off + kTmemA + a * 32, v);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) arrive_cluster(aready_rank0 + a_pub * 8);
-            return true;
-        };
-        bool ok = true;
-        for (int l = 0; l < kLead && jd < total && ok; ++l) ok = expand();
+            if (lane == 0) arrive_cluster(go_rank0 + a * 8);
+            if (ge % kSG == kSG - 1 || ge == kg - 1) ++sde;
+            if (++ge == kg) ge = 0;
+        }
+    } else {
+        // ---- scale step per group, output per tile: this warp's 32-column slice of
+        //      its lane quarter's rows ----
+        const int quad = warp & 3, cs = (warp - kSclWarp0) >> 2;
+        const int lrow = quad * 32 + lane;  // TMEM lane = tile row of this thread
+        const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+        const uint32_t d_base = tmem + lane_off + cs * kCW;
+        const uint32_t go_rank0 = peer_addr(go, 0);
+        if (lane == 0)
+            for (int b = 0; b < kDBufs; ++b) arrive_cluster(go_rank0 + b * 8);  // groups 0 .. kDBufs-1: buffers free
 
-        float* xchg = reinterpret_cast<float*>(smem + kOffXchg) + half * 64 * 64;
-        const float2 nbias = make_float2(-kBiasF, -kBiasF);
+        float* xchg = reinterpret_cast<float*>(smem + kOffXchg) + cs * kCW * 64;
         uint32_t xph = 0;
         uint32_t j = 0;
+        bool ok = true;
         for (int i = 0; i < my_tiles && ok; ++i) {
             const int t = cluster + i * nclusters;
             const int m0 = (t % p.tok_tiles) * kTok;
-            const int mbase = m0 + half * 64;
+            const int mbase = m0 + cs * kCW;
             int row, out_row;
             bool row_ok;
             if (SWI) {
@@ -450,60 +458,48 @@ __global__ void __launch_bounds__(kThreads, 1)
                 out_row = row;
             }
             const uint16_t* srow = p.s + static_cast<size_t>(row_ok ? row : 0) * kg;
-            // dx of this half's 64 tokens: lane i holds tokens mbase+i and mbase+32+i.
-            float dx_lo = 0.f, dx_hi = 0.f;
-            if (!DOTS) {
-                if (mbase + lane < p.m) dx_lo = __ldg(p.dx + mbase + lane);
-                if (mbase + 32 + lane < p.m) dx_hi = __ldg(p.dx + mbase + 32 + lane);
-            }
-            float2 acc[32];
+            // dx of this slice's tokens: lane i holds token mbase + 32 h + i in dx[h].
+            float dx[kCW / 32];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) acc[e] = make_float2(0.f, 0.f);
+            for (int h = 0; h < kCW / 32; ++h)
+                dx[h] = (!DOTS && mbase + 32 * h + lane < p.m) ? __ldg(p.dx + mbase + 32 * h + lane) : 0.f;
+            float2 acc[kCW / 2];
+#pragma unroll
+            for (int e = 0; e < kCW / 2; ++e) acc[e] = make_float2(0.f, 0.f);
 
-            // One group: expand the weights of group j + kLead, then wait for this
-            // group's accumulator, read it (re-arming the bias) and do the scale step.
+            // One group: wait for its accumulator, read it, release the buffer to the
+            // MMA of group j + kDBufs (whose first k-step overwrites it), then the
+            // scale step from registers.  The accumulator holds 16 I exactly (|16 I| <
+            // 2^22), so its conversion to f32 is exact.
             auto group = [&](int g, float sc_raw) -> bool {
-                const bool exp = jd < total;
-                if (exp && !expand_issue()) return false;
                 const uint32_t b = j % kDBufs;
-                const bool w_ok = ab.wait(gdone + j % kABufs, (j / kABufs) & 1);
+                const bool w_ok = !*abort_flag && ab.wait(gdone + j % kABufs, (j / kABufs) & 1);
                 ++j;
                 if (!__all_sync(kFull, w_ok)) return false;
                 tc_fence_after();
-                const float sc = sc_raw * 0.0625f;  // the expansion's factor 16
-                const float2 sc2 = make_float2(sc, sc);
-#pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    uint32_t r[32];
-                    const uint32_t ta = d_base + b * kTok + hh * 32;
-                    tmem_ld32(ta, r);
-                    tmem_wait_ld();
-                    tmem_bias32(ta);  // re-armed; waited for with the weight tile below
-                    if (DOTS) {
-                        if (row_ok) {
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) {
-                                const int m = mbase + hh * 32 + e;
-                                if (m < p.m)
-                                    p.dots[(static_cast<size_t>(m) * p.rows + row) * kg + g] =
-                                        static_cast<int>(r[e] - kBias) >> 4;
-                            }
-                        }
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) {
-                            const float2 f = __fadd2_rn(make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1])), nbias);
-                            acc[hh * 16 + e] = __ffma2_rn(f, sc2, acc[hh * 16 + e]);
-                        }
-                    }
-                }
-                // one wait::st and fence publish the weight tile and the re-armed accumulator
-                tmem_wait_st();
+                uint32_t r[32];
+                tmem_ld32(d_base + b * kTok, r);
+                tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) {
-                    if (exp) arrive_cluster(aready_rank0 + a_pub * 8);
-                    arrive_cluster(acce_rank0 + b * 8);
+                if (lane == 0) arrive_cluster(go_rank0 + ((j - 1 + kDBufs) % kABufs) * 8);  // group j-1+kDBufs
+                if (DOTS) {
+                    if (row_ok) {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            const int m = mbase + e;
+                            if (m < p.m) p.dots[(static_cast<size_t>(m) * p.rows + row) * kg + g] = static_cast<int>(r[e]) >> 4;
+                        }
+                    }
+                } else {
+                    const float sc = sc_raw * 0.0625f;  // the expansion's factor 16
+                    const float2 sc2 = make_float2(sc, sc);
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const float2 f = make_float2(__int2float_rn(static_cast<int>(r[2 * e])),
+                                                     __int2float_rn(static_cast<int>(r[2 * e + 1])));
+                        acc[e] = __ffma2_rn(f, sc2, acc[e]);
+                    }
                 }
                 return true;
             };
@@ -528,17 +524,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (SWI) {
                 if (lrow >= 64) {
 #pragma unroll
-                    for (int e = 0; e < 64; ++e) {
-                        const float d = __shfl_sync(kFull, e < 32 ? dx_lo : dx_hi, e & 31);
+                    for (int e = 0; e < kCW; ++e) {
+                        const float d = __shfl_sync(kFull, dx[e >> 5], e & 31);
                         const float av = (e & 1) ? acc[e >> 1].y : acc[e >> 1].x;
                         xchg[e * 64 + (lrow - 64)] = av * d;
                     }
                 }
-                if (!ab.half_sync(xbar + half, xph)) break;
+                if (!ab.slice_sync(xbar + cs, xph)) break;
                 if (lrow < 64) {
 #pragma unroll
-                    for (int e = 0; e < 64; ++e) {
-                        const float d = __shfl_sync(kFull, e < 32 ? dx_lo : dx_hi, e & 31);
+                    for (int e = 0; e < kCW; ++e) {
+                        const float d = __shfl_sync(kFull, dx[e >> 5], e & 31);
                         const int m = mbase + e;
                         if (row_ok && m < p.m) {
                             const float av = ((e & 1) ? acc[e >> 1].y : acc[e >> 1].x) * d;
@@ -546,13 +542,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
-                if (!ab.half_sync(xbar + half, xph)) break;
+                if (!ab.slice_sync(xbar + cs, xph)) break;
             } else {
-                const int mlim = p.m - mbase;  // tokens of this half that exist
+                const int mlim = p.m - mbase;  // tokens of this slice that exist
                 float* dst = p.y + static_cast<size_t>(mbase) * p.y_stride + out_row;
 #pragma unroll
-                for (int e = 0; e < 64; ++e) {
-                    const float d = __shfl_sync(kFull, e < 32 ? dx_lo : dx_hi, e & 31);
+                for (int e = 0; e < kCW; ++e) {
+                    const float d = __shfl_sync(kFull, dx[e >> 5], e & 31);
                     if (row_ok && e < mlim) {
                         const float av = ((e & 1) ? acc[e >> 1].y : acc[e >> 1].x) * d;
                         if (MODE == W4A8_ADD)
@@ -610,29 +606,32 @@ w4a8_status encode_grouped(CUtensorMap* map, const void* base, int rows, int gro
 
 template <int MODE, bool DOTS>
 w4a8_status launch_inst(const CUtensorMap& tw, const CUtensorMap& tx, const TcParams& p, cudaStream_t st) {
-    static size_t configured = 0;  // dynamic shared memory set for this instantiation
-    static int max_clusters = 0;   // clusters of this kernel that fit on the GPU at once
+    // per device: the raised shared-memory limit, and how many clusters of this
+    // kernel fit on the GPU at once
+    static FuncAttr attr;
+    static std::atomic<int> max_clusters[kMaxDevices];
     auto kernel = gemm_tc_kernel<MODE, DOTS>;
     const size_t smem = smem_bytes(MODE == W4A8_SWIGLU);
-    if (smem > configured) {
-        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        if (e != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8_gemm: smem attribute: %s", cudaGetErrorString(e));
-        configured = smem;
-    }
+    const w4a8_status a = ensure_smem(kernel, attr, smem, -1, "w4a8_gemm");
+    if (a != W4A8_OK) return a;
+    const int dev = current_device("w4a8_gemm");
+    if (dev < 0) return W4A8_ECUDA;
     cudaLaunchConfig_t cfg = {};
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = g_use_pdl ? 1 : 0;
-    cfg.attrs = attr;
+    cudaLaunchAttribute lattr[2];
+    lattr[0].id = cudaLaunchAttributeClusterDimension;
+    lattr[0].val.clusterDim.x = 2;
+    lattr[0].val.clusterDim.y = 1;
+    lattr[0].val.clusterDim.z = 1;
+    lattr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    lattr[1].val.programmaticStreamSerializationAllowed = g_use_pdl ? 1 : 0;
+    cfg.attrs = lattr;
     cfg.numAttrs = 2;
-    if (max_clusters == 0) {
+    int mc = max_clusters[dev].load(std::memory_order_acquire);
+    if (mc == 0) {
+        // a race between first calls computes the same figure twice
         cfg.gridDim = dim3(2 * (sm_count() / 2));
         int n = 0;
         const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
@@ -640,10 +639,11 @@ w4a8_status launch_inst(const CUtensorMap& tw, const CUtensorMap& tx, const TcPa
             cudaGetLastError();
             n = sm_count() / 2;
         }
-        max_clusters = n;
+        mc = n;
+        max_clusters[dev].store(mc, std::memory_order_release);
     }
     const int tiles = p.row_tiles * p.tok_tiles;
-    const int clusters = tiles < max_clusters ? tiles : max_clusters;
+    const int clusters = tiles < mc ? tiles : mc;
     cfg.gridDim = dim3(2 * clusters);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tw, tx, p);
     if (e != cudaSuccess) return set_error(W4A8_ECUDA, "w4a8_gemm (tcgen05): launch failed: %s", cudaGetErrorString(e));

@@ -58,6 +58,16 @@ __device__ __forceinline__ void cp_async_wait_upto(int n) {
     else
         asm volatile("cp.async.wait_group 2;" ::: "memory");
 }
+// Whether phase `parity` of the barrier has completed (one non-blocking test).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
 // Wait for phase `parity` of the barrier, giving up after kWaitLimitCycles: a
 // non-blocking test first (the phase is usually complete by now), then the
 // hardware-suspending try_wait, so a waiting thread does not spin on the issue port.
