@@ -394,10 +394,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sw = (lrow >> 1) & 3;  // the 64-byte swizzle of this row's chunks
         uint32_t sde = 0;                // running stage index
         int ge = 0;                      // group within the tile
+        uint32_t seen = ~0u;             // the running stage whose landing this warp has seen
+        int pend = -1;                   // the weight tile stored but not yet published
+        // A tile is published (wait::st, fence, arrival on go) once the next group's
+        // expansion is done, so each store completes while the warp works on the
+        // next group instead of holding it up.  (A store reads its registers at
+        // issue, so they are reused at once.)
+        auto publish = [&](int a) {
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) arrive_cluster(go_rank0 + a * 8);
+        };
+        bool ok = true;
         for (uint32_t jd = 0; jd < total; ++jd) {
             const uint32_t s = sde % kStages, a = jd % kABufs, ua = jd / kABufs;
-            const bool w_ok = !*abort_flag && ab.wait(full + s, (sde / kStages) & 1) && ab.wait(gdone + a, (ua & 1) ^ 1);
-            if (!__all_sync(kFull, w_ok)) break;
+            bool w_ok = !*abort_flag;
+            if (w_ok && sde != seen) {  // once per stage
+                w_ok = ab.wait(full + s, (sde / kStages) & 1);
+                seen = sde;
+            }
+            w_ok = w_ok && ab.wait(gdone + a, (ua & 1) ^ 1);
+            if (!__all_sync(kFull, w_ok)) {
+                ok = false;
+                break;
+            }
             // Packed row lrow of the group: 64 bytes in four 16-byte chunks, chunk c at
             // (c ^ sw) * 16.  A stage holds [kSG groups][128 rows][64 B]; for SWIGLU two
             // such boxes of 64 rows (gate rows, then up rows).
@@ -418,14 +439,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 v[8 * c + 6] = expand_lo(ch.w);
                 v[8 * c + 7] = expand_hi(ch.w);
             }
+            if (pend >= 0) publish(pend);
             tmem_st32(tmem + lane_off + kTmemA + a * 32, v);
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) arrive_cluster(go_rank0 + a * 8);
+            pend = static_cast<int>(a);
             if (ge % kSG == kSG - 1 || ge == kg - 1) ++sde;
             if (++ge == kg) ge = 0;
         }
+        if (ok && pend >= 0) publish(pend);
     } else {
         // ---- scale step per group, output per tile: this warp's 32-column slice of
         //      its lane quarter's rows ----
@@ -438,6 +458,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int b = 0; b < kDBufs; ++b) arrive_cluster(go_rank0 + b * 8);  // groups 0 .. kDBufs-1: buffers free
 
         float* xchg = reinterpret_cast<float*>(smem + kOffXchg) + cs * kCW * 64;
+        // the eight scales of a block in one 16-byte load: every row's scales 16-byte aligned
+        const bool vec8 = kg % 8 == 0 && (reinterpret_cast<uintptr_t>(p.s) & 15) == 0;
         uint32_t xph = 0;
         uint32_t j = 0;
         bool ok = true;
@@ -503,20 +525,38 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 return true;
             };
-            // Scales run four groups ahead of their use (an L2 round trip is several
-            // groups long), rotating through four registers so the loop stays rolled
-            // (a compact loop body keeps the instruction cache warm).
-            auto scale = [&](int g) -> float {
-                return (row_ok && g < kg) ? __half2float(__ushort_as_half(__ldg(srow + g))) : 0.f;
+            // Scales of a block of eight groups are loaded one block ahead of their
+            // use (an L2 round trip is several groups long) and the block is
+            // unrolled, so no register copy waits on a load still in flight.  One
+            // 16-byte load per block when the row's scales are 16-byte aligned.
+            auto load8 = [&](int g0, uint32_t (&d)[4]) {
+                if (vec8) {
+                    const uint4 v = (row_ok && g0 < kg) ? __ldg(reinterpret_cast<const uint4*>(srow + g0)) : make_uint4(0, 0, 0, 0);
+                    d[0] = v.x;
+                    d[1] = v.y;
+                    d[2] = v.z;
+                    d[3] = v.w;
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const uint32_t lo = (row_ok && g0 + 2 * q < kg) ? __ldg(srow + g0 + 2 * q) : 0u;
+                        const uint32_t hi = (row_ok && g0 + 2 * q + 1 < kg) ? __ldg(srow + g0 + 2 * q + 1) : 0u;
+                        d[q] = lo | (hi << 16);
+                    }
+                }
             };
-            float s0 = scale(0), s1 = scale(1), s2 = scale(2), s3 = scale(3);
+            uint32_t sc_cur[4], sc_nxt[4];
+            load8(0, sc_cur);
 #pragma unroll 1
-            for (int g = 0; g < kg && ok; ++g) {
-                ok = group(g, s0);
-                s0 = s1;
-                s1 = s2;
-                s2 = s3;
-                s3 = scale(g + 4);
+            for (int g0 = 0; g0 < kg && ok; g0 += 8) {
+                load8(g0 + 8, sc_nxt);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    if (ok && g0 + q < kg)
+                        ok = group(g0 + q, __half2float(__ushort_as_half(static_cast<unsigned short>(sc_cur[q >> 1] >> (16 * (q & 1))))));
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) sc_cur[q] = sc_nxt[q];
             }
             if (!ok || DOTS) continue;
 
