@@ -612,6 +612,10 @@ def main():
     from webyiq_b200 import _lib, ops
 
     _lib.load()
+    if local >= torch.cuda.device_count():
+        # one GPU per rank: the sharded lm_head's exchange kernels wait on each other,
+        # which ranks sharing a GPU must never do
+        raise SystemExit(f"rank {rank}: local rank {local} but only {torch.cuda.device_count()} GPU(s) visible")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if args.case:
