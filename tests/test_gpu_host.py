@@ -114,3 +114,67 @@ def test_cli_reports_truncated_shard(cuda, cli, tmp_path):
     open(shard, "wb").write(data[:-8])
     rc, out = _run(cli, d, "--bench", "1")
     assert rc == 2 and "past the end" in out, out
+
+
+def _model_oracle(layers, x, norm, ffn_norms, gate_ups, downs, head, hd, ffn, eps):
+    """The decode step's W4A8 path on the CPU oracle: per layer x += down(quant(
+    silu(g) * u)) with (g, u) = gate_up(quant(rmsnorm(x))), then the head."""
+    x = x.copy()
+    for l in range(layers):
+        xq, xs = orc.quant(x, ffn_norms[l], eps, act=1)
+        q, s = gate_ups[l]
+        h = orc.gemv(q, s, hd, 128, False, xq, xs, act=1, mode=2)
+        hq, hs = orc.quant(h, None, eps, act=1)
+        q, s = downs[l]
+        x = orc.gemv(q, s, ffn, 128, False, hq, hs, act=1, mode=1, y=x.copy())
+    xq, xs = orc.quant(x, norm, eps, act=1)
+    q, s = head
+    logits = orc.gemv(q, s, hd, 128, False, xq, xs, act=1)
+    return logits, orc.argmax(logits)
+
+
+def test_cli_ref_model(cuda, cli, tmp_path):
+    """Model-level --ref (the reference CLI's check of a whole model, main.rs:274-318)
+    on a synthetic converted model: every layer's norm + quant + SWIGLU gate_up and
+    quant + residual down, the final norm and the fused lm_head argmax, through the
+    C++ Builder and one captured graph per step, against the oracle chain: greedy
+    tokens of every step, last-step logits by cosine, max |diff| and top-10 overlap."""
+    layers, hd, ffn, vocab, steps, eps = 4, 1024, 3072, 32000, 3, 1e-6
+    tensors, ffn_norms, gate_ups, downs = {}, [], [], []
+    for l in range(layers):
+        nw = (1 + 0.1 * make_x(1, hd, seed=100 + l)[0]).astype(np.float32)
+        ffn_norms.append(nw)
+        tensors[f"l{l}.ffn_norm"] = (nw, "f32", (hd,))
+        q, s, _ = make_weight(2 * ffn, hd, 128, False, seed=200 + l)
+        gate_ups.append((q, s))
+        tensors[f"l{l}.gate_up.q"] = (q, "q4", (2 * ffn, hd))
+        tensors[f"l{l}.gate_up.s"] = (s, "f16", s.shape)
+        q, s, _ = make_weight(hd, ffn, 128, False, seed=300 + l)
+        downs.append((q, s))
+        tensors[f"l{l}.down.q"] = (q, "q4", (hd, ffn))
+        tensors[f"l{l}.down.s"] = (s, "f16", s.shape)
+    norm = (1 + 0.1 * make_x(1, hd, seed=7)[0]).astype(np.float32)
+    tensors["norm"] = (norm, "f32", (hd,))
+    q, s, _ = make_weight(vocab, hd, 128, False, seed=8)
+    head = (q, s)
+    tensors["lm_head.q"] = (q, "q4", (vocab, hd))
+    tensors["lm_head.s"] = (s, "f16", s.shape)
+    cfg = {"hidden_size": hd, "intermediate_size": ffn, "num_layers": layers, "num_heads": 8, "num_kv_heads": 8,
+           "head_dim": 128, "vocab_size": vocab, "rms_norm_eps": eps}
+    d = str(tmp_path / "model")
+    fmt.write_model(d, tensors, config=cfg, group=128, scheme="sym-rtn")
+
+    x = make_x(steps, hd, seed=9)
+    toks = []
+    for t in range(steps):
+        logits, tok = _model_oracle(layers, x[t:t + 1], norm, ffn_norms, gate_ups, downs, head, hd, ffn, eps)
+        toks.append(int(tok[0]))
+    prefix = str(tmp_path / "model_ref")
+    json.dump({"op": "model", "steps": steps}, open(prefix + ".json", "w"))
+    x.tofile(prefix + ".x.f32")
+    logits[0].astype(np.float32).tofile(prefix + ".logits.f32")
+    np.array(toks, dtype=np.uint32).tofile(prefix + ".tok.u32")
+    rc, out = _run(cli, d, "--ref", prefix)
+    assert rc == 0, out
+    assert f"greedy: {steps}/{steps} tokens match" in out, out
+    assert "top-10 overlap 10/10" in out, out

@@ -132,6 +132,19 @@ __device__ __forceinline__ void pdl_wait() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 #endif
 }
+// A load of data that an earlier kernel of the chain writes (activations, their
+// scales, logits), after pdl_wait.  A plain global load (.ca): L1 lines are
+// invalidated between dependent grids, so it sees the writes, and the warps of an
+// SM share the L1 copy of the few lines of an activation vector.  Not __ldg
+// (ld.global.nc): a kernel launched early is resident while that data is still
+// being written, which breaks the read-only contract of the non-coherent path (a
+// chain whose inputs change between steps read stale lines).  Not ld.global.cg:
+// bypassing L1, every warp of every SM requests the same L2 lines at once.
+template <typename T>
+__device__ __forceinline__ T ld_dep(const T* p) {
+    return *p;
+}
+
 __device__ __forceinline__ void pdl_launch_dependents() {
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 900
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -484,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float dx[kCW / 32];
 #pragma unroll
             for (int h = 0; h < kCW / 32; ++h)
-                dx[h] = (!DOTS && mbase + 32 * h + lane < p.m) ? __ldg(p.dx + mbase + 32 * h + lane) : 0.f;
+                dx[h] = (!DOTS && mbase + 32 * h + lane < p.m) ? ld_dep(p.dx + mbase + 32 * h + lane) : 0.f;
             float2 acc[kCW / 2];
 #pragma unroll
             for (int e = 0; e < kCW / 2; ++e) acc[e] = make_float2(0.f, 0.f);

@@ -214,12 +214,12 @@ gemv_kernel(const GemvParams p) {
         dx[t] = dxs[t] = 0.0f;
         if (t < m) {
             const uint4* xp = reinterpret_cast<const uint4*>(p.xq + static_cast<size_t>(t) * p.k) + 2 * c;
-            xa[t] = __ldg(xp);
-            xb[t] = __ldg(xp + 1);
+            xa[t] = ld_dep(xp);
+            xb[t] = ld_dep(xp + 1);
             if (EXACT) {
-                dx[t] = __ldg(p.xs + t);
+                dx[t] = ld_dep(p.xs + t);
             } else {
-                const float2 d = __ldg(reinterpret_cast<const float2*>(p.xs) + static_cast<size_t>(t) * KC + c);
+                const float2 d = ld_dep(reinterpret_cast<const float2*>(p.xs) + static_cast<size_t>(t) * KC + c);
                 dx[t] = d.x;
                 dxs[t] = d.y;
             }

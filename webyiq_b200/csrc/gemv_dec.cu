@@ -10,7 +10,7 @@
 // Why this shape (B200 view).  A decode step is a chain of such calls, each waiting
 // for the previous one (griddepcontrol.wait), so what counts is the time from that
 // wait to the last store, not bandwidth: the weights (which do not depend on the
-// previous kernel) are fetched before the wait, and after it the CTA meets no
+// previous kernel) are fetched before the wait, and after it the CTA meets one
 // barrier (two with fused quant).
 //  - One CTA per SM (two of consecutive calls fit on an SM, so the next call's
 //    copies run while this one computes) owns a balanced contiguous row range.
@@ -26,11 +26,13 @@
 //    shuffles add the row; the row's first lane writes y.  Chunks are read in a
 //    per-lane rotated order so the 8 lanes of a shared-memory phase hit distinct
 //    bank groups (rows are stored unpadded).
-//  - The activations the lane meets stay in registers (32 x GPL per token): int8
-//    activations come straight from global memory after the wait, with no CTA
-//    barrier; fused quant stages the row once per CTA in shared memory (one pass
-//    over the f32 row, the absmax exchanged by a shared atomicMax, group sums from
-//    warp shuffles) and the lanes read their chunks from there.
+//  - The activations the lane meets stay in registers (32 x GPL per token), read
+//    from a copy of the row staged once per CTA in shared memory with its group
+//    sums.  Int8 activations are copied there with one coalesced, coherent 16-byte
+//    load per piece (they are written by the previous kernel while this one is
+//    already resident, so never through the read-only path); fused quant writes the
+//    row there itself (one pass over the f32 row, the absmax exchanged by a shared
+//    atomicMax, group sums from warp shuffles).
 #include <cuda_fp16.h>
 
 #include "gemv.cuh"
@@ -211,7 +213,7 @@ __global__ void __launch_bounds__(DecCfg<MT, GPL, DEEP>::threads, DecCfg<MT, GPL
             for (int u = 0; u < VPT; ++u) {
                 const int i = tid + u * XS;
                 v[t][u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (holder && t < p.m && i < K / 4) v[t][u] = __ldg(src + i);
+                if (holder && t < p.m && i < K / 4) v[t][u] = ld_dep(src + i);
             }
         }
         if (NORM) {
@@ -291,7 +293,31 @@ __global__ void __launch_bounds__(DecCfg<MT, GPL, DEEP>::threads, DecCfg<MT, GPL
     }
     uint4 xa[MT][kSteps], xb[MT][kSteps];
     int Xg[MT][GPL];
-    if (FQ) {
+    if (!FQ) {
+        // int8 activations: staged once per CTA in shared memory, in the layout the
+        // fused quant writes, with the group sums; one coalesced 16-byte load per
+        // piece and CTA instead of every warp gathering the pieces its lanes meet.
+        const int pieces = K >> 4;  // 16-byte pieces per token; 8 per 128-group
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+            if (t >= p.m) break;
+            const uint4* src = reinterpret_cast<const uint4*>(p.xq + static_cast<size_t>(t) * K);
+            for (int base = warp * 32; base < pieces; base += T) {  // whole warps: the shuffles below
+                const int i = base + lane;
+                const bool in = i < pieces;
+                const uint4 v = in ? ld_dep(src + i) : make_uint4(0, 0, 0, 0);
+                if (in) *reinterpret_cast<uint4*>(xhalf(t, i & 1, i >> 1)) = v;
+                const uint32_t ones = 0x01010101u;
+                int X = dp4a(ones, v.x, dp4a(ones, v.y, dp4a(ones, v.z, dp4a(ones, v.w, 0))));
+                X += __shfl_xor_sync(kFull, X, 1);
+                X += __shfl_xor_sync(kFull, X, 2);
+                X += __shfl_xor_sync(kFull, X, 4);
+                if (in && (i & 7) == 0) xgrp(t)[i >> 3] = X;
+            }
+        }
+        if (tid < MT) s_dx[tid] = tid < p.m ? ld_dep(p.xs + tid) : 0.0f;
+    }
+    {
         __syncthreads();
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
@@ -306,25 +332,6 @@ __global__ void __launch_bounds__(DecCfg<MT, GPL, DEEP>::threads, DecCfg<MT, GPL
                     xa[t][c] = *reinterpret_cast<const uint4*>(xhalf(t, 0, ci));
                     xb[t][c] = *reinterpret_cast<const uint4*>(xhalf(t, 1, ci));
                 }
-            }
-        }
-    } else {
-        // int8 activations: each lane loads the chunks it meets straight from global
-        // memory (no CTA barrier) and sums its groups itself
-#pragma unroll
-        for (int t = 0; t < MT; ++t) {
-            dx[t] = t < p.m ? __ldg(p.xs + t) : 0.0f;
-#pragma unroll
-            for (int g = 0; g < GPL; ++g) Xg[t][g] = 0;
-#pragma unroll
-            for (int c = 0; c < kSteps; ++c) {
-                xa[t][c] = xb[t][c] = make_uint4(0, 0, 0, 0);
-                if (t < p.m && gin[c / 4]) {
-                    const uint4* xp = reinterpret_cast<const uint4*>(p.xq + static_cast<size_t>(t) * K + coff[c] * 2);
-                    xa[t][c] = __ldg(xp);
-                    xb[t][c] = __ldg(xp + 1);
-                }
-                Xg[t][c / 4] += chunk_sum(xa[t][c], xb[t][c]);
             }
         }
     }
@@ -426,7 +433,7 @@ bool dec_fit(const GemvParams& g, bool has_min, int mode, int threads, size_t bu
     pl.sc_off = nh * pl.rows_max * (g.k / 2);
     pl.sc_half = ((pl.rows_max * (g.k / 128) * sbytes + 15) & ~15) + 16;  // + the widening to 16 bytes
     pl.smem = static_cast<size_t>(pl.sc_off) + static_cast<size_t>(nh) * pl.sc_half +
-              (g.xf32 ? static_cast<size_t>(g.m) * (g.k + (((g.k / 128) * 4 + 15) & ~15)) : 0);  // fused quant staging
+              static_cast<size_t>(g.m) * (g.k + (((g.k / 128) * 4 + 15) & ~15));  // activation staging
     const int rows_per_pass = (pl.threads / 32) * (32 / pl.sh.L);
     const int npass = (pl.rows_max + rows_per_pass - 1) / rows_per_pass;
     const int xs = g.norm_w ? 256 : pl.threads;  // the threads that hold x (the norm's partition)

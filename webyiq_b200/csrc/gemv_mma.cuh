@@ -287,7 +287,7 @@ gemv_mma_kernel(const MmaParams p) {
                 reinterpret_cast<const float4*>(p.xf32 + static_cast<size_t>(t) * p.k + g * 128 + tq2 * 32);
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
-                const float4 v = __ldg(src + c);
+                const float4 v = ld_dep(src + c);
                 e[4 * c] = v.x;
                 e[4 * c + 1] = v.y;
                 e[4 * c + 2] = v.z;
@@ -340,7 +340,7 @@ gemv_mma_kernel(const MmaParams p) {
         }
         if (OUT != OUT_DOTS && tid < m) sdx[tid] = __fdiv_rn(__uint_as_float(s_amax_bits[tid]), 127.0f);
     } else {
-        if (OUT != OUT_DOTS && tid < m) sdx[tid] = __ldg(p.xs + tid);  // the dots hook has no xs
+        if (OUT != OUT_DOTS && tid < m) sdx[tid] = ld_dep(p.xs + tid);  // the dots hook has no xs
         const int nitem = KG * m * 4;
         for (int i0 = 0; i0 < nitem; i0 += blockDim.x) {
             const int i = i0 + tid;
@@ -348,7 +348,7 @@ gemv_mma_kernel(const MmaParams p) {
             if (i < nitem) {
                 const int tq2 = i & 3, t = (i >> 2) % m, g = (i >> 2) / m;
                 const uint4* src = reinterpret_cast<const uint4*>(p.xq + static_cast<size_t>(t) * p.k + g * 128 + tq2 * 32);
-                const uint4 u = __ldg(src), v = __ldg(src + 1);
+                const uint4 u = ld_dep(src), v = ld_dep(src + 1);
                 uint4* dst = reinterpret_cast<uint4*>(xf + static_cast<size_t>(i) * 8);
                 dst[0] = u;
                 dst[1] = v;

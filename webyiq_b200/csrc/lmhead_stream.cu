@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_stream_kernel(const Stream
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
             best[t] = 0ull;
-            dx[t] = t < p.m ? __ldg(p.xs + t) : 0.0f;
+            dx[t] = t < p.m ? ld_dep(p.xs + t) : 0.0f;
 #pragma unroll
             for (int g = 0; g < GPL; ++g) Xg[t][g] = 0;
 #pragma unroll
@@ -174,8 +174,8 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_stream_kernel(const Stream
                 xa[t][c] = xb[t][c] = make_uint4(0, 0, 0, 0);
                 if (t < p.m && gin[c / 4]) {
                     const uint4* xp = reinterpret_cast<const uint4*>(p.xq + static_cast<size_t>(t) * K + coff[c] * 2);
-                    xa[t][c] = __ldg(xp);
-                    xb[t][c] = __ldg(xp + 1);
+                    xa[t][c] = ld_dep(xp);
+                    xb[t][c] = ld_dep(xp + 1);
                 }
                 Xg[t][c / 4] += chunk_sum(xa[t][c], xb[t][c]);  // the group's activation sum
             }

@@ -41,8 +41,8 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 
 template <bool NORM>
 __device__ __forceinline__ void load8(const float* xr, const float* nw, int i, float scale, float e[8]) {
-    const float4 a = __ldg(reinterpret_cast<const float4*>(xr + i));
-    const float4 b = __ldg(reinterpret_cast<const float4*>(xr + i + 4));
+    const float4 a = ld_dep(reinterpret_cast<const float4*>(xr + i));
+    const float4 b = ld_dep(reinterpret_cast<const float4*>(xr + i + 4));
     e[0] = a.x; e[1] = a.y; e[2] = a.z; e[3] = a.w;
     e[4] = b.x; e[5] = b.y; e[6] = b.z; e[7] = b.w;
     if (NORM) {
@@ -55,7 +55,7 @@ __device__ __forceinline__ void load8(const float* xr, const float* nw, int i, f
 }
 
 template <bool NORM, int ACT>
-__global__ void __launch_bounds__(kQuantThreads) quant_kernel(const float* __restrict__ x, const float* __restrict__ nw,
+__global__ void __launch_bounds__(kQuantThreads) quant_kernel(const float* x, const float* __restrict__ nw,
                                                               float eps, int k, int8_t* __restrict__ xq,
                                                               float* __restrict__ xs) {
     __shared__ float red[kQuantThreads / 32];
@@ -69,7 +69,7 @@ __global__ void __launch_bounds__(kQuantThreads) quant_kernel(const float* __res
     if (NORM) {
         float ss = 0.0f;
         for (int i = tid * 4; i < k; i += kQuantThreads * 4) {
-            const float4 v = __ldg(reinterpret_cast<const float4*>(xr + i));
+            const float4 v = ld_dep(reinterpret_cast<const float4*>(xr + i));
             ss = __fmaf_rn(v.x, v.x, ss);
             ss = __fmaf_rn(v.y, v.y, ss);
             ss = __fmaf_rn(v.z, v.z, ss);
@@ -146,7 +146,7 @@ w4a8_status launch_quant(const float* x, const float* nw, float eps, int m, int 
 // ---------------------------------------------------------------------------
 constexpr int kArgmaxThreads = 1024;
 
-__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __restrict__ logits, int v,
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* logits, int v,
                                                                 const uint32_t* __restrict__ ids,
                                                                 uint32_t* __restrict__ tok_out) {
     __shared__ unsigned long long red[kArgmaxThreads / 32];
@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __r
     const float* lr = logits + static_cast<size_t>(blockIdx.x) * v;
     unsigned long long key = 0;
     for (int i = threadIdx.x; i < v; i += kArgmaxThreads) {
-        const unsigned long long kk = argmax_key(__ldg(lr + i), static_cast<uint32_t>(i));
+        const unsigned long long kk = argmax_key(ld_dep(lr + i), static_cast<uint32_t>(i));
         key = kk > key ? kk : key;
     }
     for (int off = 16; off > 0; off >>= 1) {

@@ -5,6 +5,9 @@
 //   webyiq_cli <model_dir> --list
 //       tensors of the manifest (no GPU needed)
 //   webyiq_cli <model_dir> --ref <prefix>
+//       <prefix>.json {"op": "model", "steps": T}: the decode step's W4A8 path over every
+//       layer of the model (see reference_model below), logits and greedy tokens
+//       checked as crates/cli/src/main.rs:274-318 checks a model; or
 //       <prefix>.json {"op": "matmul" | "quant_gemv" | "lm_head", "weight": name, "m": M,
 //                      "act": "token" | "group32", "mode": 0 | 1 | 2, "eps": e}
 //       <prefix>.x.f32  activations f32 [M, K] (quantized on the GPU)
@@ -17,6 +20,7 @@
 //   webyiq_cli <model_dir> --bench <iters>
 //       every q4 weight: GEMV (M = 1) and GEMM (M = 1024) timed with CUDA events,
 //       and all GEMVs as one captured decode-step graph
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -67,6 +71,130 @@ bool read_array(const std::string& path, std::vector<T>& out, size_t count) {
     return true;
 }
 
+// --ref op "model": the W4A8 part of a decode step over every layer of a converted
+// Llama-style model, run through the Builder and one captured graph per token, and
+// compared as the reference CLI compares a model (crates/cli/src/main.rs:274-318):
+// last-position logits (cosine, max |diff|, top 10) and the greedy tokens.
+// Per layer l (graph.rs:300-311, mlp): x += down(quant(silu(g) * u)), (g, u) =
+// gate_up(norm_quant(x, l{l}.ffn_norm)), as two fused launches (norm + quant +
+// SWIGLU GEMV, quant + residual GEMV); then head_ops (graph.rs:476-486): norm_quant(x,
+// norm), the lm_head GEMV (lm_head, or the tied embed) with the argmax fused.  The
+// attention / DeltaNet blocks are not part of this path and are not run.
+//   <prefix>.x.f32       hidden states f32 [steps, hidden] (one decode step each)
+//   <prefix>.logits.f32  expected logits of the last step f32 [vocab]
+//   <prefix>.tok.u32     expected greedy token of every step u32 [steps]
+int reference_model(Engine& e, const std::string& prefix, const Json& j) {
+    const Json& c = e.manifest().config;
+    const uint32_t layers = static_cast<uint32_t>(c["num_layers"].num);
+    const uint32_t hd = static_cast<uint32_t>(c["hidden_size"].num);
+    const uint32_t ffn = static_cast<uint32_t>(c["intermediate_size"].num);
+    const uint32_t vocab = static_cast<uint32_t>(c["vocab_size"].num);
+    const double eps = c.has("rms_norm_eps") ? c["rms_norm_eps"].num : 1e-6;
+    const uint32_t steps = j.has("steps") ? static_cast<uint32_t>(j["steps"].num) : 1;
+    if (!layers || !hd || !ffn || !vocab || !steps) return fail(Status::Error("model: config needs num_layers, hidden_size, intermediate_size, vocab_size"));
+    const std::string head = e.manifest().tensors.count("lm_head.q") ? "lm_head" : "embed";
+    const DeviceBuffer* norm = e.buffer("norm");
+    if (!norm) return fail(Status::Error("missing tensor norm"));
+    std::vector<float> x, want;
+    std::vector<uint32_t> want_tok;
+    if (!read_array(prefix + ".x.f32", x, static_cast<size_t>(steps) * hd))
+        return fail(Status::Error("bad " + prefix + ".x.f32 (want f32 [steps, hidden])"));
+    if (!read_array(prefix + ".logits.f32", want, vocab)) return fail(Status::Error("bad " + prefix + ".logits.f32"));
+    if (!read_array(prefix + ".tok.u32", want_tok, steps)) return fail(Status::Error("bad " + prefix + ".tok.u32"));
+
+    float *dx = nullptr, *dh = nullptr, *dlog = nullptr, *dxs = nullptr;
+    int8_t* dxq = nullptr;
+    uint64_t* dkey = nullptr;
+    uint32_t* dtok = nullptr;
+    void* ws = nullptr;
+    const size_t wsb = w4a8_lmhead_workspace_bytes(static_cast<int32_t>(vocab), 1);
+    CK(cudaMalloc(&dx, static_cast<size_t>(hd) * 4));
+    CK(cudaMalloc(&dh, static_cast<size_t>(ffn) * 4));
+    CK(cudaMalloc(&dlog, static_cast<size_t>(vocab) * 4));
+    CK(cudaMalloc(&dxq, hd));
+    CK(cudaMalloc(&dxs, static_cast<size_t>(hd / 32) * 8));
+    CK(cudaMalloc(&dkey, 8));
+    CK(cudaMalloc(&dtok, 4));
+    CK(cudaMalloc(&ws, wsb));
+    CK(cudaMemset(ws, 0, wsb));
+    Builder b(e);
+    Status s;
+    for (uint32_t l = 0; l < layers && s.ok(); ++l) {
+        const std::string p = "l" + std::to_string(l) + ".";
+        const DeviceBuffer* fn = e.buffer(p + "ffn_norm");
+        if (!fn) return fail(Status::Error("missing tensor " + p + "ffn_norm"));
+        s = b.quant_gemv("gate_up", p + "gate_up", hd, 2 * ffn, W4A8_SWIGLU, 1, dx, static_cast<const float*>(fn->ptr), eps, dh);
+        if (s.ok()) s = b.quant_gemv("down", p + "down", ffn, hd, W4A8_ADD, 1, dh, nullptr, eps, dx);
+    }
+    if (s.ok()) s = b.quant("norm_quant", hd, eps, dx, static_cast<const float*>(norm->ptr), 1, W4A8_ACT_TOKEN, dxq, dxs);
+    if (s.ok()) s = b.lm_head("lm_head", head, hd, 1, dxq, dxs, W4A8_ACT_TOKEN, dlog, dkey, dtok, nullptr, ws, wsb);
+    if (!s.ok()) return fail(s);
+    cudaStream_t st;
+    CK(cudaStreamCreate(&st));
+    Plan plan(b.take());
+    // one eager step sets the kernels' per-device attributes; the steps then replay the graph
+    CK(cudaMemcpyAsync(dx, x.data(), static_cast<size_t>(hd) * 4, cudaMemcpyHostToDevice, st));
+    s = plan.run(st);
+    if (s.ok()) s = plan.capture(st);
+    if (!s.ok()) return fail(s);
+    std::vector<uint32_t> got_tok(steps);
+    std::vector<float> got(vocab);
+    for (uint32_t t = 0; t < steps; ++t) {
+        CK(cudaMemcpyAsync(dx, x.data() + static_cast<size_t>(t) * hd, static_cast<size_t>(hd) * 4, cudaMemcpyHostToDevice, st));
+        s = plan.replay(st);
+        if (!s.ok()) return fail(s);
+        CK(cudaMemcpyAsync(&got_tok[t], dtok, 4, cudaMemcpyDeviceToHost, st));
+    }
+    CK(cudaMemcpyAsync(got.data(), dlog, static_cast<size_t>(vocab) * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    uint32_t code = 0;
+    if (w4a8_device_error(&code, st) != W4A8_OK) return fail(Status::Error("device error word set: a bounded wait gave up"));
+    double dot = 0, na = 0, nb = 0, maxd = 0;
+    for (uint32_t i = 0; i < vocab; ++i) {
+        dot += static_cast<double>(got[i]) * want[i];
+        na += static_cast<double>(got[i]) * got[i];
+        nb += static_cast<double>(want[i]) * want[i];
+        maxd = std::fmax(maxd, std::fabs(static_cast<double>(got[i]) - want[i]));
+    }
+    auto top = [&](const std::vector<float>& l) {
+        std::vector<uint32_t> idx(l.size());
+        for (uint32_t i = 0; i < l.size(); ++i) idx[i] = i;
+        std::partial_sort(idx.begin(), idx.begin() + std::min<size_t>(10, idx.size()), idx.end(),
+                          [&](uint32_t a, uint32_t bb) { return l[a] > l[bb] || (l[a] == l[bb] && a < bb); });
+        idx.resize(std::min<size_t>(10, idx.size()));
+        return idx;
+    };
+    const auto te = top(got), tr = top(want);
+    int shared = 0;
+    for (uint32_t a : te) shared += std::count(tr.begin(), tr.end(), a) ? 1 : 0;
+    const double cosine = dot / (std::sqrt(na) * std::sqrt(nb) + 1e-30);
+    printf("last-position logits: cosine %.6f, max |diff| %.3e, top-10 overlap %d/10\n", cosine, maxd, shared);
+    printf("  top10 engine:");
+    for (uint32_t a : te) printf(" %u", a);
+    printf("\n  top10 ref   :");
+    for (uint32_t a : tr) printf(" %u", a);
+    printf("\n");
+    uint32_t matched = 0;
+    while (matched < steps && got_tok[matched] == want_tok[matched]) ++matched;
+    printf("greedy: %u/%u tokens match reference (%u layers, hidden %u, ffn %u, vocab %u, %zu launches a step)\n",
+           matched, steps, layers, hd, ffn, vocab, plan.size());
+    printf("  engine:");
+    for (uint32_t t = 0; t < steps; ++t) printf(" %u", got_tok[t]);
+    printf("\n  ref   :");
+    for (uint32_t t = 0; t < steps; ++t) printf(" %u", want_tok[t]);
+    printf("\n");
+    cudaFree(dx);
+    cudaFree(dh);
+    cudaFree(dlog);
+    cudaFree(dxq);
+    cudaFree(dxs);
+    cudaFree(dkey);
+    cudaFree(dtok);
+    cudaFree(ws);
+    cudaStreamDestroy(st);
+    return (matched == steps && cosine >= 0.9999 && shared >= 9) ? 0 : 1;
+}
+
 int reference(Engine& e, const std::string& prefix) {
     std::vector<uint8_t> raw;
     if (!read_file(prefix + ".json", raw)) return fail(Status::Error("cannot read " + prefix + ".json"));
@@ -74,6 +202,7 @@ int reference(Engine& e, const std::string& prefix) {
     std::string err;
     if (!parse_json(std::string(raw.begin(), raw.end()), j, err)) return fail(Status::Error(prefix + ".json: " + err));
     const std::string op = j.has("op") ? j["op"].str : "matmul";
+    if (op == "model") return reference_model(e, prefix, j);
     const std::string wname = j["weight"].str;
     const uint32_t m = static_cast<uint32_t>(j["m"].num);
     const int act = j["act"].str == "group32" ? W4A8_ACT_GROUP32 : W4A8_ACT_TOKEN;
