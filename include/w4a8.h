@@ -267,6 +267,28 @@ W4A8_API w4a8_status w4a8_gather_rows(const w4a8_weight* src, const uint32_t* id
 W4A8_API w4a8_status w4a8_spec_accept(uint32_t* tok, const uint32_t* y, const uint32_t* e, const uint32_t* params,
                                      uint32_t* ctl, uint32_t* out, void* stream);
 
+/* Decode attention over an f16 KV cache, flash-decoding (attn.wgsl:41-115, the
+ * "attn" op of graph.rs:282-285): for token t of a step (at position pos + t, pos =
+ * params[0] read on the device, so a captured graph replays for every position) and
+ * each query head, softmax(q k^T / sqrt(D)) v over positions 0 ..= pos + t, in chunks
+ * of 32 positions.  qkv f32 [m, (H + 2 KVH) D] (the q heads are its first H rows of
+ * D); kc, vc f16 [KVH, maxctx, D]; query heads grouped H / KVH (<= 16) per kv head.
+ * part (f32 [m, H, maxctx / 32, D + 2]) receives each chunk's (P V, max, sum).
+ * chunks (1 .. maxctx / 32) chunks are dispatched; those past pos + t exit at once, so
+ * dispatch enough for the largest position.  D a multiple of 32 up to 1024, maxctx a
+ * multiple of 32, m in [1, W4A8_GEMV_MAX_M]; qkv, kc, vc 16-byte aligned. */
+W4A8_API w4a8_status w4a8_attn_decode(const float* qkv, const void* kc, const void* vc, int32_t H, int32_t KVH,
+                                      int32_t D, int32_t maxctx, const uint32_t* params, int32_t m, int32_t chunks,
+                                      float* part, void* stream);
+/* The merge of those chunks per query head and token (attn_combine.wgsl:31-83): the
+ * head output, times sigmoid(gate) when gsrc (f32 [m, 2 (H + KVH) D], head h's gate
+ * at h * 2D + D) is given, quantized per 32 into the W4A8_ACT_GROUP32 format of
+ * w4a8_quant: xq int8 [m, H D], xs f32 [m, H D / 32, 2] (the o projection's input).
+ * o_out (f32 [m, H, D]) or NULL receives the head outputs before quantization. */
+W4A8_API w4a8_status w4a8_attn_combine(const float* part, int32_t H, int32_t KVH, int32_t D, int32_t maxctx,
+                                       const uint32_t* params, int32_t m, const float* gsrc, int8_t* xq, float* xs,
+                                       float* o_out, void* stream);
+
 /* Index carried by a packed argmax key (0 for the "no value > -3e38" key 0). */
 static inline uint32_t w4a8_key_index(uint64_t key) {
     return key ? ~(uint32_t)(key & 0xffffffffu) : 0u;

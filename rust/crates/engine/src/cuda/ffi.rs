@@ -96,6 +96,12 @@ extern "C" {
                             dst_s: *mut c_void, stream: *mut c_void) -> w4a8_status;
     pub fn w4a8_spec_accept(tok: *mut u32, y: *const u32, e: *const u32, params: *const u32, ctl: *mut u32,
                             out: *mut u32, stream: *mut c_void) -> w4a8_status;
+    pub fn w4a8_attn_decode(qkv: *const f32, kc: *const c_void, vc: *const c_void, h: i32, kvh: i32, d: i32,
+                            maxctx: i32, params: *const u32, m: i32, chunks: i32, part: *mut f32,
+                            stream: *mut c_void) -> w4a8_status;
+    pub fn w4a8_attn_combine(part: *const f32, h: i32, kvh: i32, d: i32, maxctx: i32, params: *const u32, m: i32,
+                             gsrc: *const f32, xq: *mut i8, xs: *mut f32, o_out: *mut f32,
+                             stream: *mut c_void) -> w4a8_status;
     pub fn w4a8_group_dots(w: *const w4a8_weight, xq: *const i8, m: i32, dots: *mut i32,
                            stream: *mut c_void) -> w4a8_status;
     pub fn w4a8_gemm_group_dots(w: *const w4a8_weight, xq: *const i8, m: i32, dots: *mut i32,

@@ -133,3 +133,29 @@ def test_product_has_no_oracle_dependency():
                 text = open(os.path.join(root, f)).read()
                 for needle in ("import oracle", "from oracle", "liboracle", "orc_"):
                     assert needle not in text, (f, needle)
+
+
+def test_attention_rejects_bad_arguments_before_launch():
+    """w4a8_attn_decode / w4a8_attn_combine validate heads, head size, cache length,
+    token count, chunks and alignment on the host (no launch, no GPU)."""
+    L = _lib.load()
+    P = ctypes.c_void_p
+    good = dict(H=8, KVH=2, D=128, maxctx=1024, m=1, chunks=32)
+
+    def dec(qkv=256, kc=256, vc=256, params=256, part=256, **kw):
+        a = {**good, **kw}
+        return L.w4a8_attn_decode(P(qkv), P(kc), P(vc), a["H"], a["KVH"], a["D"], a["maxctx"], P(params), a["m"],
+                                  a["chunks"], P(part), None)
+
+    def comb(part=256, params=256, xq=256, xs=256, **kw):
+        a = {**good, **kw}
+        return L.w4a8_attn_combine(P(part), a["H"], a["KVH"], a["D"], a["maxctx"], P(params), a["m"], None, P(xq),
+                                   P(xs), None, None)
+
+    for kw in (dict(H=6, KVH=4), dict(H=34, KVH=2), dict(D=48), dict(D=2048), dict(maxctx=1000), dict(m=0),
+               dict(m=17), dict(chunks=0), dict(chunks=33), dict(params=0), dict(qkv=264), dict(kc=8), dict(part=4)):
+        assert dec(**kw) == _lib.EINVAL, kw
+        assert L.w4a8_last_error()
+    for kw in (dict(H=6, KVH=4), dict(D=48), dict(maxctx=1000), dict(m=17), dict(params=0), dict(xq=0), dict(xs=4),
+               dict(xq=2)):
+        assert comb(**kw) == _lib.EINVAL, kw

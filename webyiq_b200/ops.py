@@ -248,6 +248,35 @@ def spec_accept(tok, y, e, params, ctl, out=None):
     return tok, ctl, out
 
 
+ATTN_CHUNK = 32
+
+
+def attn_decode(qkv, kc, vc, H, KVH, D, params, m, chunks=None, part=None):
+    """Flash-decoding partials (attn.wgsl): qkv f32 [m, (H + 2 KVH) D], kc / vc f16
+    [KVH, maxctx, D], params int32 [4] on the device (pos first).  Returns part f32
+    [m, H, maxctx / 32, D + 2]; chunks defaults to all of them."""
+    _need_cuda(qkv, kc, vc, params, part)
+    maxctx = kc.shape[1]
+    nch = maxctx // ATTN_CHUNK
+    if part is None:
+        part = torch.empty((m, H, nch, D + 2), dtype=torch.float32, device=qkv.device)
+    _lib.check(_lib.load().w4a8_attn_decode(_ptr(qkv), _ptr(kc), _ptr(vc), H, KVH, D, maxctx, _ptr(params), m,
+                                            nch if chunks is None else chunks, _ptr(part), _stream()))
+    return part
+
+
+def attn_combine(part, H, KVH, D, maxctx, params, m, gsrc=None, want_o=False):
+    """The chunks merged per head (attn_combine.wgsl), times sigmoid(gate) with gsrc,
+    quantized per 32: -> (xq int8 [m, H D], xs f32 [m, H D / 32, 2], o f32 [m, H, D] or None)."""
+    _need_cuda(part, params, gsrc)
+    xq = torch.empty((m, H * D), dtype=torch.int8, device=part.device)
+    xs = torch.empty((m, H * D // 32, 2), dtype=torch.float32, device=part.device)
+    o = torch.empty((m, H, D), dtype=torch.float32, device=part.device) if want_o else None
+    _lib.check(_lib.load().w4a8_attn_combine(_ptr(part), H, KVH, D, maxctx, _ptr(params), m, _ptr(gsrc), _ptr(xq),
+                                             _ptr(xs), _ptr(o), _stream()))
+    return xq, xs, o
+
+
 XCHG_HANDLE_BYTES = 64
 
 
