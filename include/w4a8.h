@@ -289,6 +289,21 @@ W4A8_API w4a8_status w4a8_attn_combine(const float* part, int32_t H, int32_t KVH
                                        const uint32_t* params, int32_t m, const float* gsrc, int8_t* xq, float* xs,
                                        float* o_out, void* stream);
 
+/* Gated DeltaNet token mixer of a hybrid decoder's linear-attention layers
+ * (deltanet.wgsl:80-160, the "deltanet" op of graph.rs:301-310): per head of 128
+ * key and 128 value dims, the causal depthwise conv + SiLU of q/k/v, L2-normalized q
+ * and k, the gated delta rule on the head's state and the gated RMSNorm, for the m
+ * tokens of a step in order.  proj f32 [m, C + nh 128 + 2 nh] (C = 384 nh: rows
+ * q | k | v | z | b | a), conv_w f32 [C, 4] (16-byte aligned), conv_state f32
+ * [3, C, 3] and state f32 [3, nh, 128, 128] (three slots; params[3] on the device
+ * names the current one), neg_a = -exp(A_log) and dt_bias f32 [nh], gate_norm f32
+ * [128]; out f32 [m, nh 128].  spec = 0 updates the current slot in place; spec = 1
+ * (draft verification) writes the state after token t to slot (slot + 1 + t) % 3. */
+W4A8_API w4a8_status w4a8_deltanet(const float* proj, const float* conv_w, float* conv_state, float* state, float* out,
+                                   const float* neg_a, const float* dt_bias, const float* gate_norm,
+                                   const uint32_t* params, int32_t nh, int32_t m, float eps, int32_t spec,
+                                   void* stream);
+
 /* Index carried by a packed argmax key (0 for the "no value > -3e38" key 0). */
 static inline uint32_t w4a8_key_index(uint64_t key) {
     return key ? ~(uint32_t)(key & 0xffffffffu) : 0u;

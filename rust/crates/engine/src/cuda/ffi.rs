@@ -102,6 +102,9 @@ extern "C" {
     pub fn w4a8_attn_combine(part: *const f32, h: i32, kvh: i32, d: i32, maxctx: i32, params: *const u32, m: i32,
                              gsrc: *const f32, xq: *mut i8, xs: *mut f32, o_out: *mut f32,
                              stream: *mut c_void) -> w4a8_status;
+    pub fn w4a8_deltanet(proj: *const f32, conv_w: *const f32, conv_state: *mut f32, state: *mut f32, out: *mut f32,
+                         neg_a: *const f32, dt_bias: *const f32, gate_norm: *const f32, params: *const u32, nh: i32,
+                         m: i32, eps: f32, spec: i32, stream: *mut c_void) -> w4a8_status;
     pub fn w4a8_group_dots(w: *const w4a8_weight, xq: *const i8, m: i32, dots: *mut i32,
                            stream: *mut c_void) -> w4a8_status;
     pub fn w4a8_gemm_group_dots(w: *const w4a8_weight, xq: *const i8, m: i32, dots: *mut i32,

@@ -159,3 +159,16 @@ def test_attention_rejects_bad_arguments_before_launch():
     for kw in (dict(H=6, KVH=4), dict(D=48), dict(maxctx=1000), dict(m=17), dict(params=0), dict(xq=0), dict(xs=4),
                dict(xq=2)):
         assert comb(**kw) == _lib.EINVAL, kw
+
+
+def test_deltanet_rejects_bad_arguments_before_launch():
+    L = _lib.load()
+    P = ctypes.c_void_p
+
+    def call(nh=4, m=1, conv_w=256, proj=256):
+        return L.w4a8_deltanet(P(proj), P(conv_w), P(256), P(256), P(256), P(256), P(256), P(256), P(256), nh, m,
+                               1e-6, 0, None)
+
+    for kw in (dict(nh=0), dict(m=0), dict(m=17), dict(conv_w=8), dict(proj=0)):
+        assert call(**kw) == _lib.EINVAL, kw
+        assert L.w4a8_last_error()

@@ -56,6 +56,7 @@ _SIGS = {
     "w4a8_spec_accept": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P]),
     "w4a8_attn_decode": (ctypes.c_int, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _I, _P, _P]),
     "w4a8_attn_combine": (ctypes.c_int, [_P, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P, _P]),
+    "w4a8_deltanet": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, ctypes.c_float, _I, _P]),
     "w4a8_nccl_get_unique_id": (ctypes.c_int, [_P]),
     "w4a8_nccl_comm_init": (ctypes.c_int, [_I, _P, _I, ctypes.POINTER(ctypes.c_void_p)]),
     "w4a8_nccl_comm_destroy": (ctypes.c_int, [_P]),

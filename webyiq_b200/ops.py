@@ -277,6 +277,19 @@ def attn_combine(part, H, KVH, D, maxctx, params, m, gsrc=None, want_o=False):
     return xq, xs, o
 
 
+def deltanet(proj, conv_w, conv_state, state, neg_a, dt_bias, gate_norm, params, nh, m, eps=1e-6, spec=False,
+             out=None):
+    """Gated DeltaNet mixer (deltanet.wgsl) on device f32 tensors; conv_state and state
+    (three slots each) are updated in place.  Returns out f32 [m, nh * 128]."""
+    _need_cuda(proj, conv_w, conv_state, state, neg_a, dt_bias, gate_norm, params, out)
+    if out is None:
+        out = torch.empty((m, nh * 128), dtype=torch.float32, device=proj.device)
+    _lib.check(_lib.load().w4a8_deltanet(_ptr(proj), _ptr(conv_w), _ptr(conv_state), _ptr(state), _ptr(out),
+                                         _ptr(neg_a), _ptr(dt_bias), _ptr(gate_norm), _ptr(params), nh, m, eps,
+                                         1 if spec else 0, _stream()))
+    return out
+
+
 XCHG_HANDLE_BYTES = 64
 
 
