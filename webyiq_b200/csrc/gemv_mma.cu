@@ -63,14 +63,17 @@ w4a8_status launch_mode(const MmaParams& p, int mode, int out, cudaStream_t st) 
 
 }  // namespace
 
-// GemvParams -> tensor-core launches in token blocks of 8.
+// GemvParams -> tensor-core launches: outputs into y take up to 16 tokens a launch
+// (two mma blocks of 8 over one pass of the weights); the argmax and the group-dot
+// hook take 8.
 w4a8_status launch_gemv_mma(const GemvParams& g, bool has_min, int mode, int out, cudaStream_t st) {
     const int kg = g.k / 128;
-    for (int t0 = 0; t0 < g.m; t0 += kMmaTokens) {
+    const int step = out == OUT_Y ? kMmaMaxTokens : kMmaTokens;
+    for (int t0 = 0; t0 < g.m; t0 += step) {
         MmaParams p{};
         p.q = g.q;
         p.s = g.s;
-        p.m = g.m - t0 < kMmaTokens ? g.m - t0 : kMmaTokens;
+        p.m = g.m - t0 < step ? g.m - t0 : step;
         p.xq = g.xq ? g.xq + static_cast<size_t>(t0) * g.k : nullptr;
         p.xf32 = g.xf32 ? g.xf32 + static_cast<size_t>(t0) * g.k : nullptr;
         p.xs = g.xs ? g.xs + t0 : nullptr;

@@ -38,7 +38,8 @@ namespace w4a8 {
 
 constexpr int kMmaMaxWarps = 16;
 constexpr int kMmaGPS = 4;      // groups per K-slice task
-constexpr int kMmaTokens = 8;   // tokens per launch (the mma N)
+constexpr int kMmaTokens = 8;   // tokens of one mma block (the mma N)
+constexpr int kMmaMaxTokens = 16;  // tokens per launch: the 8-token kernel runs two blocks over one weight pass
 constexpr int kMmaMaxStages = 3;
 
 // Set (atomicOr) by a kernel whose bounded wait gave up; read and cleared by
@@ -94,8 +95,8 @@ __host__ __device__ inline MmaSmem mma_smem_plan(int m, int k, int rt, int ks, i
     s.xf = up(s.sc + stages * s.sc_bytes);
     s.xg = s.xf + kg * m * 4 * 32;
     s.dx = up(s.xg + kg * m * 4);                       // per-token dx [8]
-    s.red = up(s.dx + kMmaTokens * 4);
-    s.bar = up(s.red + static_cast<size_t>(rt) * ks * 16 * kMmaTokens * 8);
+    s.red = up(s.dx + kMmaMaxTokens * 4);
+    s.bar = up(s.red + static_cast<size_t>(rt) * ks * 16 * kMmaMaxTokens * 8);
     s.total = s.bar + kMmaMaxStages * 8;
     return s;
 }
@@ -126,7 +127,10 @@ gemv_mma_kernel(const MmaParams p) {
     const int lane = tid & 31, warp = tid >> 5;
     const int gq = lane >> 2, tq = lane & 3;  // mma group / thread-in-group
     const int KC = p.k >> 5, KG = p.k >> 7;
-    const int m = MT < p.m ? MT : p.m;  // MT: compile-time bound on the tokens
+    // MT: compile-time bound on the tokens of one mma block; the 8-token kernel takes
+    // up to 16 tokens as two blocks that share each staged weight round
+    const int m = MT == kMmaTokens ? min(p.m, kMmaMaxTokens) : min(MT, p.m);
+    const int nblk = (m + kMmaTokens - 1) / kMmaTokens;
     const int rt = p.rt, ks = p.ks, S = p.stages;
     const int tile = warp / ks, slice = warp - tile * ks;  // this warp's task
     const bool active = tile < rt;
@@ -233,10 +237,10 @@ gemv_mma_kernel(const MmaParams p) {
 
     // Fused quant: per-token absmax, as float bits (non-negative, so they order
     // as unsigned integers), filled by shared-memory atomicMax.
-    __shared__ unsigned int s_amax_bits[kMmaTokens];
+    __shared__ unsigned int s_amax_bits[kMmaMaxTokens];
     __shared__ uint4 s_xzero[2];  // the activations a B column meets outside its slot
     if (tid < 2) s_xzero[tid] = make_uint4(0, 0, 0, 0);
-    if (FQ && tid < kMmaTokens) s_amax_bits[tid] = 0u;
+    if (FQ && tid < kMmaMaxTokens) s_amax_bits[tid] = 0u;
 
     // Weights first: they do not depend on the previous kernel.  Each thread waits
     // for its own pieces of round 0 before the dependency wait.
@@ -382,6 +386,8 @@ gemv_mma_kernel(const MmaParams p) {
         const int ric = SWI ? rows_round + ria : ria + 8;
         const unsigned char* rowa = st + static_cast<size_t>(tile * 16 + gq) * stride + tq * 16;
         const unsigned char* rowc = rowa + static_cast<size_t>(8) * stride;
+        for (int tb = 0; tb < nblk; ++tb) {  // token blocks of 8 (one unless MT == 8 and m > 8)
+        const int tb0 = tb * kMmaTokens, mb = m - tb0;  // this block's first token, tokens left
         // two accumulators per set (by group parity) when a set takes several
         // groups, so that the dependent mma chains stay short
         constexpr int NSUB = NSLOT > 1 ? 2 : 1;
@@ -402,8 +408,8 @@ gemv_mma_kernel(const MmaParams p) {
                 wc = *reinterpret_cast<const uint4*>(rowc + g * 64);
             }
             // B column gq: token btok's activations if group j is in its slot
-            const bool mine = (j % NSLOT) == bslot && btok < m;
-            const uint4* xp = mine ? reinterpret_cast<const uint4*>(xf + ((static_cast<size_t>(g) * m + btok) * 4 + tq) * 8)
+            const bool mine = (j % NSLOT) == bslot && btok < mb;
+            const uint4* xp = mine ? reinterpret_cast<const uint4*>(xf + ((static_cast<size_t>(g) * m + tb0 + btok) * 4 + tq) * 8)
                                    : s_xzero;
             const uint4 x0 = xp[0];  // activations of k-words 0, 1 (low 4, high 4 each)
             const uint4 x1 = xp[1];  // k-words 2, 3
@@ -429,14 +435,14 @@ gemv_mma_kernel(const MmaParams p) {
             for (int e = 0; e < 4; ++e) {
                 if (MT == 1 && (e & 1)) continue;  // both D columns hold token 0
                 const int t = MT == 1 ? 0 : (2 * tq + (e & 1)) % MT;
-                if (t >= m) continue;
+                if (t >= mb) continue;
                 int lo = dl[a][0][e], hi = dh[a][0][e];
                 if (NSUB == 2) {
                     lo += dl[a][NSUB - 1][e];
                     hi += dh[a][NSUB - 1][e];
                 }
                 const int I = lo + (hi >> 4);  // hi = 16 * high-nibble dot, exact
-                const int X = xg[g * m + t];
+                const int X = xg[g * m + tb0 + t];
                 uint32_t s;
                 if (scale_tma) {
                     const size_t si = static_cast<size_t>(e < 2 ? ria : ric) * KG + g;
@@ -448,7 +454,7 @@ gemv_mma_kernel(const MmaParams p) {
                 if (OUT == OUT_DOTS) {
                     const bool ok = e < 2 ? oka : okc;
                     const int row = e < 2 ? ra : rc;
-                    if (ok) p.dots[(static_cast<size_t>(t) * p.n_out + row) * KG + g] = HAS_MIN ? I : I - 8 * X;
+                    if (ok) p.dots[(static_cast<size_t>(tb0 + t) * p.n_out + row) * KG + g] = HAS_MIN ? I : I - 8 * X;
                 } else if (HAS_MIN) {
                     const Fix16 fs = fix16(s & 0xffffu), fm = fix16(s >> 16);
                     acc[e] += shl64(fs.mant * I, fs.sh) + shl64(fm.mant * X, fm.sh);
@@ -467,7 +473,6 @@ gemv_mma_kernel(const MmaParams p) {
                 acc[e] += shfl_xor_i64(acc[e], 2);
             }
         }
-        if (r + 1 < rounds) load_scales(r + 1);  // in flight during the sums below
         const bool writer = MT <= 2 ? tq == 0 : (MT == 4 ? tq < 2 : true);
         if (OUT != OUT_DOTS && active && writer) {  // K-slice partial sums: red[tile][slice][A row][token]
 #pragma unroll
@@ -475,9 +480,11 @@ gemv_mma_kernel(const MmaParams p) {
                 if (MT == 1 && (e & 1)) continue;
                 const int t = MT == 1 ? 0 : (2 * tq + (e & 1)) % MT;
                 const int arow = gq + (e >= 2 ? 8 : 0);
-                if (t < m) red[((static_cast<size_t>(tile) * ks + slice) * 16 + arow) * kMmaTokens + t] = acc[e];
+                if (t < mb) red[((static_cast<size_t>(tile) * ks + slice) * 16 + arow) * kMmaMaxTokens + tb0 + t] = acc[e];
             }
         }
+        }  // token blocks
+        if (r + 1 < rounds) load_scales(r + 1);
         __syncthreads();  // every warp is done with stage `slot` and has stored its sums
         if (r + S < rounds) issue(r + S, slot);
         if (OUT == OUT_DOTS) continue;
@@ -488,8 +495,8 @@ gemv_mma_kernel(const MmaParams p) {
             const int tl = orow / TR, rw = orow - tl * TR;
             long long a0 = 0, a1 = 0;
             for (int s2 = 0; s2 < ks; ++s2) {
-                a0 += red[((static_cast<size_t>(tl) * ks + s2) * 16 + rw) * kMmaTokens + t];
-                if (SWI) a1 += red[((static_cast<size_t>(tl) * ks + s2) * 16 + rw + 8) * kMmaTokens + t];
+                a0 += red[((static_cast<size_t>(tl) * ks + s2) * 16 + rw) * kMmaMaxTokens + t];
+                if (SWI) a1 += red[((static_cast<size_t>(tl) * ks + s2) * 16 + rw + 8) * kMmaMaxTokens + t];
             }
             const float dx = sdx[t];
             const float v0 = fix_to_float(a0, dx);
