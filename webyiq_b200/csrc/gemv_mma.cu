@@ -9,31 +9,55 @@ int sm_count();  // capi.cu
 namespace {
 
 // One CTA per SM (fewer when rows are scarce) on balanced row ranges; a round is
-// RT tiles of 16 rows (8 output rows for SWIGLU); RT x KS warps, KS = ceil(KG/4).
-template <bool HAS_MIN, int MODE, int OUT, int MT, bool FQ>
-w4a8_status launch_mt(MmaParams p, cudaStream_t st) {
-    static FuncAttr attr;  // set on first use per device: static shared memory counts against the default 48 KB too
-    auto kernel = gemv_mma_kernel<HAS_MIN, MODE, OUT, MT, FQ>;
+// RT tiles of 16 rows (8 output rows for SWIGLU); RT x KS warps, KS = ceil(KG/4),
+// at most max_warps.  Fills p.ks, p.rt, p.stages and the shared-memory plan; false
+// when no plan fits in smem_cap bytes.
+bool configure(MmaParams& p, bool swi, bool has_min, int max_warps, size_t smem_cap, int& ctas, MmaSmem& plan) {
     const int kg = p.k / 128;
     p.ks = (kg + kMmaGPS - 1) / kMmaGPS;
-    if (p.ks > kMmaMaxWarps) return set_error(W4A8_EINVAL, "w4a8 gemv: k=%d too large", p.k);
-    const int tr = MODE == W4A8_SWIGLU ? 8 : 16;
+    if (p.ks > max_warps) return false;
+    const int tr = swi ? 8 : 16;
     const int sms = sm_count();
-    int ctas = (p.n_out + 7) / 8;
+    ctas = (p.n_out + 7) / 8;
     if (ctas > sms) ctas = sms;
     if (ctas < 1) ctas = 1;
     const int rows = (p.n_out + ctas - 1) / ctas;
     int rt = (rows + tr - 1) / tr;
-    const int rt_max = kMmaMaxWarps / p.ks;
+    const int rt_max = max_warps / p.ks;
     if (rt > rt_max) rt = rt_max;
     p.rt = rt < 1 ? 1 : rt;
     const int rounds = (rows + p.rt * tr - 1) / (p.rt * tr);
     p.stages = rounds < kMmaMaxStages ? rounds : kMmaMaxStages;
-    const int sb = HAS_MIN ? 4 : 2;
-    MmaSmem plan = mma_smem_plan(p.m, p.k, p.rt, p.ks, p.stages, sb);
-    while (plan.total > 227 * 1024 && p.stages > 1) plan = mma_smem_plan(p.m, p.k, p.rt, p.ks, --p.stages, sb);
-    while (plan.total > 227 * 1024 && p.rt > 1) plan = mma_smem_plan(p.m, p.k, --p.rt, p.ks, p.stages, sb);
-    if (plan.total > 227 * 1024) return set_error(W4A8_EINVAL, "w4a8 gemv: shared memory plan too large");
+    const int sb = has_min ? 4 : 2;
+    plan = mma_smem_plan(p.m, p.k, p.rt, p.ks, p.stages, sb);
+    while (plan.total > smem_cap && p.stages > 1) plan = mma_smem_plan(p.m, p.k, p.rt, p.ks, --p.stages, sb);
+    while (plan.total > smem_cap && p.rt > 1) plan = mma_smem_plan(p.m, p.k, --p.rt, p.ks, p.stages, sb);
+    return plan.total <= smem_cap;
+}
+
+template <bool HAS_MIN, int MODE, int OUT, int MT, bool FQ>
+w4a8_status launch_mt(MmaParams p, cudaStream_t st) {
+    constexpr bool SWI = MODE == W4A8_SWIGLU;
+    int ctas = 0;
+    MmaSmem plan{};
+    // Several tokens into y: the two-CTAs-an-SM kernel when a plan of at most 12
+    // warps fits twice in an SM
+    if constexpr (MT > 1 && !HAS_MIN && OUT == OUT_Y && !FQ) {
+        MmaParams q = p;
+        if (configure(q, SWI, HAS_MIN, kMmaPairWarps, kMmaPairSmem, ctas, plan)) {
+            static FuncAttr attr;
+            auto kernel = gemv_mma_kernel<HAS_MIN, MODE, OUT, MT, FQ, true>;
+            const w4a8_status a = ensure_smem(kernel, attr, plan.total, 100, "w4a8 gemv (mma)");
+            if (a != W4A8_OK) return a;
+            return launch_pdl("w4a8 gemv (mma)", kernel, dim3(ctas), dim3(q.rt * q.ks * 32), plan.total, st, q);
+        }
+    }
+    static FuncAttr attr;  // set on first use per device: static shared memory counts against the default 48 KB too
+    auto kernel = gemv_mma_kernel<HAS_MIN, MODE, OUT, MT, FQ>;
+    if (!configure(p, SWI, HAS_MIN, kMmaMaxWarps, 227 * 1024, ctas, plan)) {
+        if (p.ks > kMmaMaxWarps) return set_error(W4A8_EINVAL, "w4a8 gemv: k=%d too large", p.k);
+        return set_error(W4A8_EINVAL, "w4a8 gemv: shared memory plan too large");
+    }
     const w4a8_status a = ensure_smem(kernel, attr, plan.total, -1, "w4a8 gemv (mma)");
     if (a != W4A8_OK) return a;
     return launch_pdl("w4a8 gemv (mma)", kernel, dim3(ctas), dim3(p.rt * p.ks * 32), plan.total, st, p);

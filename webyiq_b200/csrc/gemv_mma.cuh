@@ -80,7 +80,7 @@ __host__ __device__ inline int mma_row_stride(int k) {
 // Shared memory: weight stages [S][rt*16 rows][stride], their scales
 // [S][rt*16 rows][k/128] (rows in the order they are copied), activation operands
 // [KG][m][4][8 words] (the 32 bytes lane-quarter t meets), per-group activation
-// sums [KG][m], K-slice partial sums [rt][ks][16][8] (int64).
+// sums [KG][m], K-slice partial sums [rt][ks][16][m] (int64).
 struct MmaSmem {
     size_t stage, stage_bytes, sc, sc_bytes, xf, xg, dx, red, bar, total;
 };
@@ -96,7 +96,7 @@ __host__ __device__ inline MmaSmem mma_smem_plan(int m, int k, int rt, int ks, i
     s.xg = s.xf + kg * m * 4 * 32;
     s.dx = up(s.xg + kg * m * 4);                       // per-token dx [8]
     s.red = up(s.dx + kMmaMaxTokens * 4);
-    s.bar = up(s.red + static_cast<size_t>(rt) * ks * 16 * kMmaMaxTokens * 8);
+    s.bar = up(s.red + static_cast<size_t>(rt) * ks * 16 * m * 8);
     s.total = s.bar + kMmaMaxStages * 8;
     return s;
 }
@@ -109,15 +109,22 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, 
 }
 
 // One token: 64 registers, so the next kernel's CTA fits beside this one and its
-// TMA copies start while this one finishes.  More tokens: room for the epilogue.
-template <int MT>
+// weight copies start while this one finishes.  More tokens: room for the epilogue,
+// unless PAIR: at most 12 warps and 80 registers, so that two CTAs (this call's and
+// the next one's) share an SM whenever the shared-memory plan fits twice.
+constexpr int kMmaPairWarps = 12;
+// dynamic shared bytes of a PAIR CTA: two of them, with their static arrays (< 512
+// bytes) and the 1 KB the runtime reserves a CTA, fit in an SM's 228 KB
+constexpr size_t kMmaPairSmem = 228 * 1024 / 2 - 1024 - 512;
+template <int MT, bool PAIR>
 struct MmaBounds {
-    static constexpr int min_blocks = MT == 1 ? 2 : 1;
+    static constexpr int threads = PAIR ? kMmaPairWarps * 32 : kMmaMaxWarps * 32;
+    static constexpr int min_blocks = (MT == 1 || PAIR) ? 2 : 1;
 };
 
 // FQ: the activations arrive as f32 (p.xf32) and are quantized per token here.
-template <bool HAS_MIN, int MODE, int OUT, int MT, bool FQ>
-__global__ void __launch_bounds__(kMmaMaxWarps * 32, MmaBounds<MT>::min_blocks)
+template <bool HAS_MIN, int MODE, int OUT, int MT, bool FQ, bool PAIR = false>
+__global__ void __launch_bounds__(MmaBounds<MT, PAIR>::threads, MmaBounds<MT, PAIR>::min_blocks)
 gemv_mma_kernel(const MmaParams p) {
     constexpr bool SWI = (MODE == W4A8_SWIGLU);
     constexpr int TR = SWI ? 8 : 16;  // output rows per tile
@@ -480,7 +487,7 @@ gemv_mma_kernel(const MmaParams p) {
                 if (MT == 1 && (e & 1)) continue;
                 const int t = MT == 1 ? 0 : (2 * tq + (e & 1)) % MT;
                 const int arow = gq + (e >= 2 ? 8 : 0);
-                if (t < mb) red[((static_cast<size_t>(tile) * ks + slice) * 16 + arow) * kMmaMaxTokens + tb0 + t] = acc[e];
+                if (t < mb) red[((static_cast<size_t>(tile) * ks + slice) * 16 + arow) * m + tb0 + t] = acc[e];
             }
         }
         }  // token blocks
@@ -495,8 +502,8 @@ gemv_mma_kernel(const MmaParams p) {
             const int tl = orow / TR, rw = orow - tl * TR;
             long long a0 = 0, a1 = 0;
             for (int s2 = 0; s2 < ks; ++s2) {
-                a0 += red[((static_cast<size_t>(tl) * ks + s2) * 16 + rw) * kMmaMaxTokens + t];
-                if (SWI) a1 += red[((static_cast<size_t>(tl) * ks + s2) * 16 + rw + 8) * kMmaMaxTokens + t];
+                a0 += red[((static_cast<size_t>(tl) * ks + s2) * 16 + rw) * m + t];
+                if (SWI) a1 += red[((static_cast<size_t>(tl) * ks + s2) * 16 + rw + 8) * m + t];
             }
             const float dx = sdx[t];
             const float v0 = fix_to_float(a0, dx);
