@@ -352,22 +352,36 @@ gemv_mma_kernel(const MmaParams p) {
         if (OUT != OUT_DOTS && tid < m) sdx[tid] = __fdiv_rn(__uint_as_float(s_amax_bits[tid]), 127.0f);
     } else {
         if (OUT != OUT_DOTS && tid < m) sdx[tid] = ld_dep(p.xs + tid);  // the dots hook has no xs
+        // Up to four items a thread are requested before any is used, so that a
+        // pass costs one round trip, not one per item (one token: one item a thread).
+        constexpr int kIt = MT == 1 ? 1 : 4;
         const int nitem = KG * m * 4;
-        for (int i0 = 0; i0 < nitem; i0 += blockDim.x) {
-            const int i = i0 + tid;
-            int X = 0;
-            if (i < nitem) {
-                const int tq2 = i & 3, t = (i >> 2) % m, g = (i >> 2) / m;
-                const uint4* src = reinterpret_cast<const uint4*>(p.xq + static_cast<size_t>(t) * p.k + g * 128 + tq2 * 32);
-                const uint4 u = ld_dep(src), v = ld_dep(src + 1);
-                uint4* dst = reinterpret_cast<uint4*>(xf + static_cast<size_t>(i) * 8);
-                dst[0] = u;
-                dst[1] = v;
-                X = chunk_sum(u, v);
+        for (int i0 = 0; i0 < nitem; i0 += kIt * blockDim.x) {
+            uint4 u[kIt], v[kIt];
+#pragma unroll
+            for (int b = 0; b < kIt; ++b) {
+                const int i = i0 + b * blockDim.x + tid;
+                if (i < nitem) {
+                    const int tq2 = i & 3, t = (i >> 2) % m, g = (i >> 2) / m;
+                    const uint4* src = reinterpret_cast<const uint4*>(p.xq + static_cast<size_t>(t) * p.k + g * 128 + tq2 * 32);
+                    u[b] = ld_dep(src);
+                    v[b] = ld_dep(src + 1);
+                }
             }
-            X += __shfl_xor_sync(kFull, X, 1);
-            X += __shfl_xor_sync(kFull, X, 2);
-            if (i < nitem && (i & 3) == 0) xg[i >> 2] = X;  // [g][t]
+#pragma unroll
+            for (int b = 0; b < kIt; ++b) {
+                const int i = i0 + b * blockDim.x + tid;
+                int X = 0;
+                if (i < nitem) {
+                    uint4* dst = reinterpret_cast<uint4*>(xf + static_cast<size_t>(i) * 8);
+                    dst[0] = u[b];
+                    dst[1] = v[b];
+                    X = chunk_sum(u[b], v[b]);
+                }
+                X += __shfl_xor_sync(kFull, X, 1);
+                X += __shfl_xor_sync(kFull, X, 2);
+                if (i < nitem && (i & 3) == 0) xg[i >> 2] = X;  // [g][t]
+            }
         }
     }
     __syncthreads();
@@ -405,6 +419,50 @@ gemv_mma_kernel(const MmaParams p) {
             for (int u = 0; u < NSUB; ++u)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) dl[a][u][e] = dh[a][u][e] = 0;
+        // the exact per-group scale step of this lane's groups of set a; element e:
+        // A row gq (e < 2) or gq+8, D column 2tq + (e & 1) = token (2tq + (e & 1)) % MT
+        long long acc[4] = {0, 0, 0, 0};
+        auto finish = [&](int a) {
+            const int jj = a * NSLOT + dslot;
+            if (jj >= ng) return;
+            const int gg = g0 + jj;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                if (MT == 1 && (e & 1)) continue;  // both D columns hold token 0
+                const int t = MT == 1 ? 0 : (2 * tq + (e & 1)) % MT;
+                if (t >= mb) continue;
+                int lo = dl[a][0][e], hi = dh[a][0][e];
+                if (NSUB == 2) {
+                    lo += dl[a][NSUB - 1][e];
+                    hi += dh[a][NSUB - 1][e];
+                }
+                const int I = lo + (hi >> 4);  // hi = 16 * high-nibble dot, exact
+                const int X = xg[gg * m + tb0 + t];
+                uint32_t s;
+                if (scale_tma) {
+                    const size_t si = static_cast<size_t>(e < 2 ? ria : ric) * KG + gg;
+                    s = HAS_MIN ? reinterpret_cast<const uint32_t*>(scs)[si]
+                                : static_cast<uint32_t>(reinterpret_cast<const unsigned short*>(scs)[si]);
+                } else {
+                    s = e < 2 ? sa[a] : sc[a];
+                }
+                if (OUT == OUT_DOTS) {
+                    const bool ok = e < 2 ? oka : okc;
+                    const int row = e < 2 ? ra : rc;
+                    if (ok) p.dots[(static_cast<size_t>(tb0 + t) * p.n_out + row) * KG + gg] = HAS_MIN ? I : I - 8 * X;
+                } else if (HAS_MIN) {
+                    const Fix16 fs = fix16(s & 0xffffu), fm = fix16(s >> 16);
+                    acc[e] += shl64(fs.mant * I, fs.sh) + shl64(fm.mant * X, fm.sh);
+                } else {
+                    const Fix16 fs = fix16(s);
+                    acc[e] += shl64(fs.mant * (I - 8 * X), fs.sh);
+                }
+            }
+        };
+        // one group a set (8 tokens): each set is finished right after its mma, so
+        // that its accumulators die early (four live sets would spill); otherwise
+        // all sets after the last mma
+        constexpr bool EARLY = NSLOT == 1;
 #pragma unroll
         for (int j = 0; j < kMmaGPS; ++j) {
             if (j >= ng) break;
@@ -429,47 +487,11 @@ gemv_mma_kernel(const MmaParams p) {
             mma_u8s8(sl, wa.z & ml, wc.z & ml, wa.w & ml, wc.w & ml, x1.x, x1.z);
             mma_u8s8(sh, wa.x & mh, wc.x & mh, wa.y & mh, wc.y & mh, x0.y, x0.w);
             mma_u8s8(sh, wa.z & mh, wc.z & mh, wa.w & mh, wc.w & mh, x1.y, x1.w);
+            if (EARLY) finish(j);
         }
-        // the exact per-group scale step of this lane's groups; element e: A row gq
-        // (e < 2) or gq+8, D column 2tq + (e & 1) = token (2tq + (e & 1)) % MT
-        long long acc[4] = {0, 0, 0, 0};
+        if (!EARLY) {
 #pragma unroll
-        for (int a = 0; a < NSET; ++a) {
-            const int j = a * NSLOT + dslot;
-            if (j >= ng) continue;
-            const int g = g0 + j;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                if (MT == 1 && (e & 1)) continue;  // both D columns hold token 0
-                const int t = MT == 1 ? 0 : (2 * tq + (e & 1)) % MT;
-                if (t >= mb) continue;
-                int lo = dl[a][0][e], hi = dh[a][0][e];
-                if (NSUB == 2) {
-                    lo += dl[a][NSUB - 1][e];
-                    hi += dh[a][NSUB - 1][e];
-                }
-                const int I = lo + (hi >> 4);  // hi = 16 * high-nibble dot, exact
-                const int X = xg[g * m + tb0 + t];
-                uint32_t s;
-                if (scale_tma) {
-                    const size_t si = static_cast<size_t>(e < 2 ? ria : ric) * KG + g;
-                    s = HAS_MIN ? reinterpret_cast<const uint32_t*>(scs)[si]
-                                : static_cast<uint32_t>(reinterpret_cast<const unsigned short*>(scs)[si]);
-                } else {
-                    s = e < 2 ? sa[a] : sc[a];
-                }
-                if (OUT == OUT_DOTS) {
-                    const bool ok = e < 2 ? oka : okc;
-                    const int row = e < 2 ? ra : rc;
-                    if (ok) p.dots[(static_cast<size_t>(tb0 + t) * p.n_out + row) * KG + g] = HAS_MIN ? I : I - 8 * X;
-                } else if (HAS_MIN) {
-                    const Fix16 fs = fix16(s & 0xffffu), fm = fix16(s >> 16);
-                    acc[e] += shl64(fs.mant * I, fs.sh) + shl64(fm.mant * X, fm.sh);
-                } else {
-                    const Fix16 fs = fix16(s);
-                    acc[e] += shl64(fs.mant * (I - 8 * X), fs.sh);
-                }
-            }
+            for (int a = 0; a < NSET; ++a) finish(a);
         }
         // lanes of a quad holding the same rows and tokens (other groups) add up
         if (OUT != OUT_DOTS && MT <= 4) {
