@@ -218,13 +218,18 @@ W4A8_API w4a8_status w4a8_nccl_comm_destroy(void* comm);
  * in its GPU memory; every rank opens every other rank's buffer through a CUDA IPC
  * handle (W4A8_XCHG_HANDLE_BYTES bytes, passed between the processes by the host,
  * e.g. an all-gather over torch.distributed).  A call then runs the shard's
- * lm_head argmax and one exchange kernel: it stores the rank's keys into every
- * peer's buffer, raises its per-call sequence flag there, waits (bounded) for all
- * ranks' flags and takes the max, so every rank gets the key and token of the
- * global argmax, bit-identical to one GPU, without NCCL.  The key slots are
- * double-buffered by the sequence's parity and the sequence counter lives on the
- * device, so the calls can be captured in a CUDA graph; every rank must make the
- * same number of calls with the same m (<= W4A8_XCHG_MAX_TOKENS).  A wait that
+ * lm_head argmax and the exchange: the rank's keys, tagged with the call's
+ * sequence number, are stored into every peer's buffer, and once every rank's keys
+ * of the call are in (bounded waits) their max gives every rank the key and token
+ * of the global argmax, bit-identical to one GPU, without NCCL.  Where the
+ * streaming lm_head covers the shard (group 128, per-token, one or two tokens,
+ * whole 8-row blocks) its last CTA runs the exchange, so a call is one kernel;
+ * otherwise a small exchange kernel follows.  The vocabulary ids of the shard
+ * (row_offset + row) must lie below 2^24: the tag lives in the top 8 bits of the
+ * key's id half.  The key slots are double-buffered by the sequence's parity and
+ * the sequence counter lives on the device, so the calls can be captured in a CUDA
+ * graph; every rank must make the same number of calls with the same m
+ * (<= W4A8_XCHG_MAX_TOKENS).  A wait that
  * gives up (a peer ~0.3 s late, e.g. stalled on its host) leaves this rank's own
  * keys in best_key and sets the device error word, and the call itself still
  * returns W4A8_OK: callers must check w4a8_device_error (W4A8_ETIMEOUT) after their

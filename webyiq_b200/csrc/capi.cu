@@ -8,6 +8,7 @@
 
 #include "gemv.cuh"
 #include "launch.cuh"
+#include "xchg.cuh"
 
 namespace w4a8 {
 
@@ -74,6 +75,10 @@ w4a8_status launch_gemv_mma(const GemvParams& g, bool has_min, int mode, int out
 bool gemv_dec_covers(const GemvParams& g, int group, int act, int mode, int out);
 w4a8_status launch_gemv_dec(const GemvParams& g, bool has_min, int mode, cudaStream_t st);
 bool lmhead_stream_covers(const GemvParams& g, int group, int act);
+w4a8_status lmhead_argmax_impl(const w4a8_weight* w, int32_t row_offset, const int8_t* xq, const float* xs,
+                               int32_t act, int32_t m, float* logits, uint64_t* best_key, uint32_t* tok_out,
+                               const uint32_t* ids, void* workspace, size_t workspace_bytes, void* stream,
+                               const XchgArgs* x, bool* fused);
 w4a8_status launch_lmhead_stream(const GemvParams& g, bool has_min, cudaStream_t st);
 w4a8_status device_error(unsigned int* code, cudaStream_t st);
 w4a8_status selftest_wait_timeout(cudaStream_t st);
@@ -317,6 +322,18 @@ size_t w4a8_lmhead_workspace_bytes(int32_t n, int32_t m) {
 w4a8_status w4a8_lmhead_argmax(const w4a8_weight* w, int32_t row_offset, const int8_t* xq, const float* xs,
                                int32_t act, int32_t m, float* logits, uint64_t* best_key, uint32_t* tok_out,
                                const uint32_t* ids, void* workspace, size_t workspace_bytes, void* stream) {
+    return lmhead_argmax_impl(w, row_offset, xq, xs, act, m, logits, best_key, tok_out, ids, workspace,
+                              workspace_bytes, stream, nullptr, nullptr);
+}
+
+}  // extern "C"
+
+namespace w4a8 {
+
+w4a8_status lmhead_argmax_impl(const w4a8_weight* w, int32_t row_offset, const int8_t* xq, const float* xs,
+                               int32_t act, int32_t m, float* logits, uint64_t* best_key, uint32_t* tok_out,
+                               const uint32_t* ids, void* workspace, size_t workspace_bytes, void* stream,
+                               const XchgArgs* x, bool* fused) {
     w4a8_status st = check_weight(w, "w4a8_lmhead_argmax");
     if (st != W4A8_OK) return st;
     if ((st = check_act(xq, xs, act, "w4a8_lmhead_argmax")) != W4A8_OK) return st;
@@ -334,14 +351,19 @@ w4a8_status w4a8_lmhead_argmax(const w4a8_weight* w, int32_t row_offset, const i
     p.counter = static_cast<unsigned int*>(workspace);
     p.ws_best = reinterpret_cast<unsigned long long*>(static_cast<char*>(workspace) + 128);
     p.best_key = reinterpret_cast<unsigned long long*>(best_key);
-    p.tok_out = tok_out;
     p.ids = ids;
     p.n_out = w->n;
     p.y_stride = w->n;
     p.k = w->k;
     p.m = m;
     p.row_offset = row_offset;
+    // with an exchange, the streaming kernel merges in its last CTA; any other
+    // kernel leaves the shard's key and no token for the merge kernel
+    const bool fuse = x && x->world > 0 && g_use_mma && lmhead_stream_covers(p, w->group, act);
+    if (fused) *fused = fuse;
+    p.xchg = fuse ? x : nullptr;
+    p.tok_out = (x && !fuse) ? nullptr : tok_out;
     return launch_gemv(p, w->group, w->has_min != 0, act, W4A8_STORE, OUT_ARGMAX, static_cast<cudaStream_t>(stream));
 }
 
-}  // extern "C"
+}  // namespace w4a8

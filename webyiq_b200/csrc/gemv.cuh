@@ -45,6 +45,8 @@ __host__ __device__ constexpr int gemv_u(int nr) { return nr == 2 ? 8 : kGemvU; 
 constexpr int kGemvMaxMT = 4;    // tokens per launch; more tokens = more launches
 constexpr int kGemvMaxKC = 256;  // k <= 8192
 
+struct XchgArgs;  // xchg.cuh
+
 struct GemvParams {
     const uint4* q;        // [rows, k/32] 16-byte chunks
     const void* s;         // scales, see w4a8.h
@@ -65,6 +67,7 @@ struct GemvParams {
     int m;          // tokens in this launch (<= kGemvMaxMT)
     int y_stride;   // token stride of y (n_out of the full call)
     int row_offset; // OUT_ARGMAX: global id of row 0
+    const XchgArgs* xchg;  // OUT_ARGMAX, streaming kernel only: merge the keys over peers in the last CTA (or null)
 };
 
 // Segment = the lanes whose group terms are summed by shuffles before they are

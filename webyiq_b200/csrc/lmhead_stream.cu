@@ -30,13 +30,16 @@
 //  - A warp releases a stage with one shared atomic; no CTA-wide barrier runs per
 //    stage.  At the end the CTA's best key per token goes through the same
 //    workspace protocol as w4a8_lmhead_argmax (atomicMax, done counter, the last
-//    CTA publishes and re-zeroes).
+//    CTA publishes and re-zeroes).  For a vocabulary shard of the column-split
+//    lm_head (w4a8_lmhead_argmax_xchg) the last CTA instead merges the keys with
+//    the peers over NVLink (xchg.cuh), so the sharded call is one kernel.
 // Every wait is bounded; a wait that gives up sets the device error word.
 #include <cuda_fp16.h>
 
 #include "gemv.cuh"
 #include "launch.cuh"
 #include "tma.cuh"
+#include "xchg.cuh"
 
 namespace w4a8 {
 
@@ -66,6 +69,7 @@ struct StreamParams {
     int n, k, m, row_offset;
     int rows_per_stage;    // R, a multiple of 8
     uint32_t stage_bytes;  // R * k/2 + the scale span, 128-byte multiple
+    XchgArgs xchg;         // world > 0: the last CTA merges the keys over the peers (xchg.cuh)
 };
 
 // Lanes per row (L) and groups per lane (GPL) for kg groups per row and mt tokens:
@@ -102,6 +106,7 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_stream_kernel(const Stream
     __shared__ unsigned long long s_key[kConsumers][MT];
     __shared__ bool s_last;
     __shared__ volatile int s_abort;
+    __shared__ unsigned int s_xseq;  // the exchange's sequence number (shards of a column-split head)
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = p.k, KG = K >> 7;
@@ -159,6 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_stream_kernel(const Stream
         for (int c = 0; c < kSteps; ++c) coff[c] = (gidx[c / 4] * 4 + (c % 4 + rc) % 4) * 16;
 
         pdl_wait();  // the activations come from the previous kernel
+        if (p.xchg.world > 0 && tid == 0) s_xseq = xchg_next_seq(p.xchg);  // off the merge's critical path
         uint4 xa[MT][kSteps], xb[MT][kSteps];
         int Xg[MT][GPL];
         float dx[MT];
@@ -308,6 +314,16 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_stream_kernel(const Stream
     __syncthreads();
     if (s_last) {
         __threadfence();
+        if (p.xchg.world > 0) {
+            // the shard's key goes straight into the exchange with the peers, so a
+            // sharded call is this one kernel
+            __shared__ unsigned long long s_own[MT];
+            if (tid < p.m) s_own[tid] = atomicExch(p.ws_best + tid, 0ull);
+            if (tid == 0) *p.counter = 0u;
+            __syncthreads();
+            xchg_merge(p.xchg, p.m, s_xseq, s_own, p.best_key, p.tok_out, p.ids, p.err);
+            return;
+        }
         if (tid < p.m) {
             const unsigned long long key = atomicExch(p.ws_best + tid, 0ull);
             p.best_key[tid] = key;
@@ -374,6 +390,7 @@ w4a8_status launch_lmhead_stream(const GemvParams& g, bool has_min, cudaStream_t
     p.k = g.k;
     p.m = g.m;
     p.row_offset = g.row_offset;
+    if (g.xchg) p.xchg = *g.xchg;
     const SpanShape sh = span_shape(g.k / 128, g.m);
     if (sh.L == 0) return set_error(W4A8_EINVAL, "w4a8 lm_head (stream): k=%d not covered", g.k);
     p.rows_per_stage = stream_rows(g.k, sh.L);
