@@ -369,8 +369,8 @@ def run_extras(torch, ops, dev, steps, warmup, world, rank, dist):
     out["c3_lmhead_argmax"] = {"gpus": world, "c3_parity": c3_parity, "us_per_token": round(ms * 1e3, 2), "tok_s": round(1e3 / ms, 1),
                                "gbs_total": round(lm_bytes / (ms * 1e-3) / 1e9, 1),
                                "frac_hbm_per_gpu": round(lm_bytes / world / (ms * 1e-3) / 1e9 / hbm, 3),
-                               "collective": "w4a8_lmhead_argmax_xchg: packed keys stored into every peer's "
-                                             "buffer over NVLink, one flag per rank, in one kernel"
+                               "collective": "w4a8_lmhead_argmax_xchg: packed keys tagged with the call, stored "
+                                             "into every peer's buffer over NVLink by the lm_head kernel's last CTA"
                                              if world > 1 else None,
                                "us_per_token_nccl_allreduce": round(ms_nccl * 1e3, 2) if ms_nccl else None,
                                "timing": f"CUDA graph of {C3_CALLS} calls (one token each), PDL between them"}
