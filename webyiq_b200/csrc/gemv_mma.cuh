@@ -426,6 +426,33 @@ gemv_mma_kernel(const MmaParams p) {
             const int jj = a * NSLOT + dslot;
             if (jj >= ng) return;
             const int gg = g0 + jj;
+            // the raw scale words of rows gq and gq+8 for this group
+            uint32_t s2[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (scale_tma) {
+                    const size_t si = static_cast<size_t>(h == 0 ? ria : ric) * KG + gg;
+                    s2[h] = HAS_MIN ? reinterpret_cast<const uint32_t*>(scs)[si]
+                                    : static_cast<uint32_t>(reinterpret_cast<const unsigned short*>(scs)[si]);
+                } else {
+                    s2[h] = h == 0 ? sa[a] : sc[a];
+                }
+            }
+            // fix(s) = mant * 2^sh as one int64 per row, so that a step is one wide
+            // multiply-add: D * (mant << sh) == (mant * D) << sh exactly (|mant * D| <
+            // 2^28, |result| < 2^58)
+            long long fsc[2] = {0, 0}, fmn[2] = {0, 0};
+            if (OUT != OUT_DOTS) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const Fix16 fs = fix16(HAS_MIN ? (s2[h] & 0xffffu) : s2[h]);
+                    fsc[h] = shl64(fs.mant, fs.sh);
+                    if (HAS_MIN) {
+                        const Fix16 fm = fix16(s2[h] >> 16);
+                        fmn[h] = shl64(fm.mant, fm.sh);
+                    }
+                }
+            }
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 if (MT == 1 && (e & 1)) continue;  // both D columns hold token 0
@@ -438,24 +465,14 @@ gemv_mma_kernel(const MmaParams p) {
                 }
                 const int I = lo + (hi >> 4);  // hi = 16 * high-nibble dot, exact
                 const int X = xg[gg * m + tb0 + t];
-                uint32_t s;
-                if (scale_tma) {
-                    const size_t si = static_cast<size_t>(e < 2 ? ria : ric) * KG + gg;
-                    s = HAS_MIN ? reinterpret_cast<const uint32_t*>(scs)[si]
-                                : static_cast<uint32_t>(reinterpret_cast<const unsigned short*>(scs)[si]);
-                } else {
-                    s = e < 2 ? sa[a] : sc[a];
-                }
                 if (OUT == OUT_DOTS) {
                     const bool ok = e < 2 ? oka : okc;
                     const int row = e < 2 ? ra : rc;
                     if (ok) p.dots[(static_cast<size_t>(tb0 + t) * p.n_out + row) * KG + gg] = HAS_MIN ? I : I - 8 * X;
                 } else if (HAS_MIN) {
-                    const Fix16 fs = fix16(s & 0xffffu), fm = fix16(s >> 16);
-                    acc[e] += shl64(fs.mant * I, fs.sh) + shl64(fm.mant * X, fm.sh);
+                    acc[e] += static_cast<long long>(I) * fsc[e >> 1] + static_cast<long long>(X) * fmn[e >> 1];
                 } else {
-                    const Fix16 fs = fix16(s);
-                    acc[e] += shl64(fs.mant * (I - 8 * X), fs.sh);
+                    acc[e] += static_cast<long long>(I - 8 * X) * fsc[e >> 1];
                 }
             }
         };
