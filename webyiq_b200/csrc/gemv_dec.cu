@@ -41,7 +41,8 @@
 
 namespace w4a8 {
 
-int sm_count();  // capi.cu
+int sm_count();
+unsigned int* device_error_word();  // gemv_mma.cu
 
 namespace {
 
@@ -77,6 +78,7 @@ struct DecParams {
     int rows_max;  // rows of the largest CTA range
     int sc_off;    // shared-memory offset of the scale spans (per half: sc_half bytes)
     int sc_half;
+    unsigned int* err;  // device error word
 };
 
 __device__ __forceinline__ int pack_fix(uint32_t h) {
@@ -154,7 +156,12 @@ __global__ void __launch_bounds__(DecCfg<MT, GPL, DEEP>::threads, DecCfg<MT, GPL
     }
     __shared__ unsigned int s_amax[2];  // fused quant: per-token absmax as float bits
     __shared__ float s_dx[2];
+    __shared__ uint64_t s_xbar;         // int8 activations: their bulk copy landed
     if (FQ && tid < 2) s_amax[tid] = 0u;
+    if (!FQ && tid == 0) {
+        mbar_init(&s_xbar, 1);
+        mbar_init_fence();
+    }
     cp_async_wait_upto(0);  // this thread's pieces have landed
     __syncthreads();        // and everyone's
     // decoded scales (and mins) of this lane's groups, [pass][h][g]
@@ -295,17 +302,29 @@ __global__ void __launch_bounds__(DecCfg<MT, GPL, DEEP>::threads, DecCfg<MT, GPL
     int Xg[MT][GPL];
     if (!FQ) {
         // int8 activations: staged once per CTA in shared memory, in the layout the
-        // fused quant writes, with the group sums; one coalesced 16-byte load per
-        // piece and CTA instead of every warp gathering the pieces its lanes meet.
+        // fused quant writes, with the group sums.  The rows come in by one bulk copy
+        // issued after the dependency wait: it goes through the TMA unit, not behind
+        // the weight copies that the next calls' CTAs on this SM have queued at the
+        // load/store unit.  Then one 16-byte shared-memory read per piece.
         const int pieces = K >> 4;  // 16-byte pieces per token; 8 per 128-group
+        unsigned char* raw = xsm + static_cast<size_t>(p.m) * xrow;  // [m][K], after the staging rows
+        if (tid == 0) {
+            mbar_expect_tx(&s_xbar, static_cast<uint32_t>(p.m * K));
+            tma_bulk_load(raw, p.xq, static_cast<uint32_t>(p.m * K), &s_xbar);
+        }
+        if (tid < MT) s_dx[tid] = tid < p.m ? ld_dep(p.xs + tid) : 0.0f;
+        if (!mbar_wait(&s_xbar, 0)) {
+            atomicOr(p.err, DEV_ERR_TMA_TIMEOUT);
+            mbar_wait(&s_xbar, 0);  // once more (bounded), so the copy is not in flight at exit
+        }
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
             if (t >= p.m) break;
-            const uint4* src = reinterpret_cast<const uint4*>(p.xq + static_cast<size_t>(t) * K);
+            const uint4* src = reinterpret_cast<const uint4*>(raw + static_cast<size_t>(t) * K);
             for (int base = warp * 32; base < pieces; base += T) {  // whole warps: the shuffles below
                 const int i = base + lane;
                 const bool in = i < pieces;
-                const uint4 v = in ? ld_dep(src + i) : make_uint4(0, 0, 0, 0);
+                const uint4 v = in ? src[i] : make_uint4(0, 0, 0, 0);
                 if (in) *reinterpret_cast<uint4*>(xhalf(t, i & 1, i >> 1)) = v;
                 const uint32_t ones = 0x01010101u;
                 int X = dp4a(ones, v.x, dp4a(ones, v.y, dp4a(ones, v.z, dp4a(ones, v.w, 0))));
@@ -315,7 +334,6 @@ __global__ void __launch_bounds__(DecCfg<MT, GPL, DEEP>::threads, DecCfg<MT, GPL
                 if (in && (i & 7) == 0) xgrp(t)[i >> 3] = X;
             }
         }
-        if (tid < MT) s_dx[tid] = tid < p.m ? ld_dep(p.xs + tid) : 0.0f;
     }
     {
         __syncthreads();
@@ -433,7 +451,8 @@ bool dec_fit(const GemvParams& g, bool has_min, int mode, int threads, size_t bu
     pl.sc_off = nh * pl.rows_max * (g.k / 2);
     pl.sc_half = ((pl.rows_max * (g.k / 128) * sbytes + 15) & ~15) + 16;  // + the widening to 16 bytes
     pl.smem = static_cast<size_t>(pl.sc_off) + static_cast<size_t>(nh) * pl.sc_half +
-              static_cast<size_t>(g.m) * (g.k + (((g.k / 128) * 4 + 15) & ~15));  // activation staging
+              static_cast<size_t>(g.m) * (g.k + (((g.k / 128) * 4 + 15) & ~15)) +  // activation staging
+              (g.xf32 ? 0 : static_cast<size_t>(g.m) * g.k);                        // and its bulk copy
     const int rows_per_pass = (pl.threads / 32) * (32 / pl.sh.L);
     const int npass = (pl.rows_max + rows_per_pass - 1) / rows_per_pass;
     const int xs = g.norm_w ? 256 : pl.threads;  // the threads that hold x (the norm's partition)
@@ -512,6 +531,10 @@ w4a8_status launch_gemv_dec(const GemvParams& g, bool has_min, int mode, cudaStr
     p.rows_max = pl.rows_max;
     p.sc_off = pl.sc_off;
     p.sc_half = pl.sc_half;
+    p.err = device_error_word();
+    if (!p.err) return set_error(W4A8_ECUDA, "w4a8 gemv (decode): device error word unavailable");
+    if (!g.xf32 && (reinterpret_cast<uintptr_t>(g.xq) & 15) != 0)
+        return set_error(W4A8_EINVAL, "w4a8 gemv (decode): xq not 16-byte aligned");
     if (g.xf32 && g.norm_w)
         return has_min ? dec_mode_dispatch<true, true, true>(p, pl, mode, st)
                        : dec_mode_dispatch<false, true, true>(p, pl, mode, st);
